@@ -1,0 +1,424 @@
+"""Benchmark of the b200_paged attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--dtype fp16|bf16] [--ctx uniform|fixed4096]
+
+Workload (Qwen3-0.6B attention shape): 256 decode
+sequences per GPU, context lengths uniform in [512, 4096] (or all 4096),
+16 query / 8 KV heads, head_dim 128, block_size 16, N(0,1) K/V in ONE
+layer's paged cache sized to 80% of HBM, block tables drawn at random
+without replacement over the whole pool.  A step is one
+``AttentionOperator.forward`` — the KV scatter of the step's new tokens and
+split-KV paged decode over the whole context.  Each GPU holds its own pool
+and its own 256 sequences (whole sequences are partitioned over GPUs, no
+collective on the data path): weak scaling.
+
+Metric: algorithmic HBM bytes of paged decode per second (GB/s) —
+sum(ctx) * Hkv * D * 2 (K and V) * elsize + Q and O (2 * B * Hq * D * elsize)
++ block-table entries (8 B per page).  Inputs are larger than L2 (about
+2.4 GB of KV per step against a 126 MB L2), so no flush is needed.
+
+``--impl reference`` times the reference algorithm on the host CPU (the
+numpy port in oracle/, all host threads) on a bounded sample of the same
+workload and reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM, BLOCK_SIZE = 16, 8, 128, 16
+BATCH_PER_GPU = 256
+POOL_FRACTION = 0.8
+
+
+def parse_args() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--dtype", choices=("fp16", "bf16"), default="fp16")
+    ap.add_argument("--ctx", choices=("uniform", "fixed4096"), default="uniform")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def context_lengths(mode: str, n: int, seed: int) -> list[int]:
+    from micro_vllm_b200.workloads import uniform_lengths
+
+    return [4096] * n if mode == "fixed4096" else uniform_lengths(n, 512, 4096, seed)
+
+
+def decode_bytes(ctx: list[int], elsize: int) -> int:
+    """Algorithmic HBM bytes of one paged decode launch."""
+
+    kv = sum(ctx) * NUM_KV_HEADS * HEAD_DIM * 2 * elsize
+    qo = 2 * len(ctx) * NUM_Q_HEADS * HEAD_DIM * elsize
+    table = sum(-(-c // BLOCK_SIZE) for c in ctx) * 8
+    return kv + qo + table
+
+
+def write_bytes(n: int, elsize: int) -> int:
+    """Algorithmic bytes of the KV scatter: read new K/V, write them."""
+
+    return 2 * 2 * n * NUM_KV_HEADS * HEAD_DIM * elsize
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks during the timed region."""
+
+    FIELDS = (
+        "clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower() in ("active", "1", "yes"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx or None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ---------------------------------------------------------------- CPU
+def cpu_baseline(args, dtype_size: int, seconds: float) -> dict:
+    """The reference algorithm (numpy port of ReferenceAttentionOperator,
+    oracle/paged_attention.py) on the host cores, on a bounded sample: the
+    first sequences of the same workload, repeated for about `seconds`."""
+
+    import numpy as np
+
+    from oracle import build_metadata, paged_attention
+
+    cores = os.cpu_count() or 1
+    sample = 32
+    ctx = context_lengths(args.ctx, BATCH_PER_GPU, seed=0)[:sample]
+    rng = np.random.default_rng(0)
+    tables, cursor = [], 0
+    for c in ctx:
+        n = -(-c // BLOCK_SIZE)
+        tables.append(list(range(cursor, cursor + n)))
+        cursor += n
+    cache = rng.standard_normal((2, cursor, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
+    md = build_metadata([[c - 1] for c in ctx], tables, block_size=BLOCK_SIZE)
+    q = rng.standard_normal((sample, NUM_Q_HEADS, HEAD_DIM), dtype=np.float32)
+    k = rng.standard_normal((sample, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
+    v = rng.standard_normal((sample, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
+    from threadpoolctl import threadpool_limits
+
+    # Requests run on `cores` threads; one BLAS thread each avoids oversubscription.
+    with threadpool_limits(limits=1):
+        paged_attention(q, k, v, cache, md, num_threads=cores)  # warm-up
+        calls, t0 = 0, time.perf_counter()
+        while True:
+            paged_attention(q, k, v, cache, md, num_threads=cores)
+            calls += 1
+            elapsed = time.perf_counter() - t0
+            if elapsed >= seconds or calls >= 1000:
+                break
+    per_call = elapsed / calls
+    return {
+        "value": decode_bytes(ctx, dtype_size) / per_call / 1e9,
+        "unit": "GB/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": (
+            f"{sample} of the {BATCH_PER_GPU} decode sequences ({args.ctx} ctx), fp32 numpy port of "
+            f"ReferenceAttentionOperator, {calls} calls in {elapsed:.1f}s, "
+            f"{per_call * 1e3:.1f} ms/call; bytes counted at {dtype_size}-byte elements like the GPU line"
+        ),
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    elsize = 2
+    cpu = cpu_baseline(args, elsize, seconds=max(2.0, args.cpu_sample_seconds / 2))
+    # Steps: repeated bounded samples; time each as one step.
+    values = []
+    for _ in range(max(1, min(args.steps, 3))):
+        values.append(cpu_baseline(args, elsize, seconds=2.0)["value"])
+    value = statistics.median(values + [cpu["value"]])
+    line = {
+        "impl": "reference",
+        "metric": "paged_decode_hbm_GBps",
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"config2 paged decode, 256 seqs/GPU, ctx {args.ctx}, 16/8 heads, D128, bs16",
+            "sample_sequences": 32,
+        },
+        "cpu_baseline": cpu,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from micro_vllm_b200 import AttentionMetadata, B200PagedAttentionOperator
+    from micro_vllm_b200 import _lib
+    from micro_vllm_b200.workloads import paged_batch, pool_blocks_for_fraction
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
+    elsize = 2
+
+    ctx = context_lengths(args.ctx, BATCH_PER_GPU, seed=1000 + rank)
+    nb = pool_blocks_for_fraction(POOL_FRACTION, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, dtype, dev)
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=[1] * BATCH_PER_GPU, num_q_heads=NUM_Q_HEADS,
+        num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE, num_blocks=nb,
+        dtype=dtype, device=dev, seed=2000 + rank,
+    )
+    op = B200PagedAttentionOperator()
+    op.reserve(dev, max_num_tokens=BATCH_PER_GPU, max_num_requests=BATCH_PER_GPU,
+               num_q_heads=NUM_Q_HEADS, num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    step = lambda: op(batch.query, batch.key, batch.value, batch.cache, batch.metadata)  # noqa: E731
+
+    # Attention-only entry point (plan + decode), to time the decode kernel.
+    md = batch.metadata
+    ws, st = op._workspace(dev, BATCH_PER_GPU, BATCH_PER_GPU, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM)
+    out_buf = torch.empty_like(batch.query)
+    lib = _lib.load()
+    attn_args = (
+        batch.query.data_ptr(), batch.query.stride(0), batch.query.stride(1), out_buf.data_ptr(),
+        batch.cache.data_ptr(), nb, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM,
+        md.query_positions.data_ptr(), md.query_context_start_positions.data_ptr(),
+        md.query_start_locations.data_ptr(), md.context_lengths.data_ptr(),
+        md.block_table.data_ptr(), md.block_table.stride(0), md.block_table.shape[1],
+        BATCH_PER_GPU, BATCH_PER_GPU, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
+        _lib.MVB_DTYPE_F16 if dtype == torch.float16 else _lib.MVB_DTYPE_BF16,
+        ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream,
+    )
+
+    def attention_only() -> None:
+        _lib.check(lib.mvb_paged_attention(*attn_args), "bench attention")
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+        attention_only()
+    barrier()
+
+    # ---- timed region: K full forward steps ----
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    t_start.record(stream)
+    for _ in range(args.steps):
+        step()
+    t_stop.record(stream)
+    barrier()
+    step_ms = max_over_ranks(t_start.elapsed_time(t_stop) / args.steps)
+
+    # ---- decode kernel alone (plan + decode launches) ----
+    barrier()
+    a_start, a_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a_start.record(stream)
+    for _ in range(args.steps):
+        attention_only()
+    a_stop.record(stream)
+    barrier()
+    clock_info = clocks.stop()
+    attn_ms = max_over_ranks(a_start.elapsed_time(a_stop) / args.steps)
+
+    # ---- end to end through the public operator with host buffers ----
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    host = {
+        "q": pin(batch.query), "k": pin(batch.key), "v": pin(batch.value),
+        "pos": pin(md.query_positions), "start": pin(md.query_context_start_positions),
+        "qsl": pin(md.query_start_locations), "ctx": pin(md.context_lengths),
+        "table": pin(md.block_table), "slots": pin(md.slot_mapping),
+    }
+    out_host = torch.empty(batch.query.shape, dtype=dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step() -> None:
+        d = {k: t.to(dev, non_blocking=True) for k, t in host.items()}
+        emd = AttentionMetadata(
+            query_positions=d["pos"], query_context_start_positions=d["start"],
+            query_start_locations=d["qsl"], context_lengths=d["ctx"], block_table=d["table"],
+            slot_mapping=d["slots"], block_size=BLOCK_SIZE,
+        )
+        out = op(d["q"], d["k"], d["v"], batch.cache, emd)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_stop.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.steps)
+
+    attn_bytes = decode_bytes(ctx, elsize)
+    step_bytes_all = attn_bytes * world  # every rank runs the same-size workload
+    value = step_bytes_all / (step_ms * 1e-3) / 1e9
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peak, peak_src = 6650.0, "fallback"
+    if peaks_path.exists():
+        peak, peak_src = float(json.loads(peaks_path.read_text())["hbm_gbs"]), "measured"
+    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    line = {
+        "metric": "paged_decode_hbm_GBps",
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16" if dtype == torch.float16 else "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": (
+                f"BASELINE config 2: paged decode, {BATCH_PER_GPU} seqs/GPU, ctx "
+                f"{'U[512,4096]' if args.ctx == 'uniform' else '4096'}, Hq 16 / Hkv 8, D 128, bs 16, "
+                f"pool {POOL_FRACTION:.0%} of HBM ({nb} blocks), random block tables; step = KV scatter + decode"
+            ),
+            "global_batch": BATCH_PER_GPU * world,
+            "parallelism": f"sequence-partitioned replicas x{world}",
+            "l2": "inputs larger than L2 (KV per step about %.2f GB vs 126 MB L2); no flush" % (attn_bytes / 1e9),
+            "bytes_per_step_per_gpu": attn_bytes,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "peak_source": peak_src,
+            "kernel": "paged_decode_kernel (timed with its planner launch, attention-only entry point)",
+            "ms_per_launch": attn_ms,
+        },
+        "e2e": {
+            "value": step_bytes_all / (e2e_ms * 1e-3) / 1e9,
+            "unit": "GB/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": e2e_ms,
+        },
+        "gpu_launches": 4 * args.steps,
+        "clocks": clock_info,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, elsize, args.cpu_sample_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,145 @@
+/*
+ * mvb200.h — C ABI of the B200 (sm_100a) paged-attention backend for
+ * micro-vLLM.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and
+ * a cudaStream_t passed as `void*`; none allocates memory, synchronises the
+ * host or takes a torch type.  All work is enqueued on `stream`, so the
+ * calls can be issued from any host language and captured in a CUDA graph
+ * once the workspace exists.  Return value: MVB_OK or a negative MVB_ERR_*.
+ *
+ * Tensor layouts (element offsets, 64-bit everywhere):
+ *   kv_cache   [2, num_blocks, block_size, num_kv_heads, head_dim], contiguous
+ *              (plane 0 = keys, plane 1 = values) — the layout ModelRunner
+ *              allocates (model_runner.py:678-703 in the reference project).
+ *   query      [num_tokens, num_q_heads, head_dim], innermost stride 1.
+ *   key/value  [num_tokens, num_kv_heads, head_dim], any strides.
+ *   output     [num_tokens, num_q_heads, head_dim], contiguous.
+ *   metadata   int64 device arrays with the meaning of the reference's
+ *              AttentionMetadata (attention/attention.py:12-28).
+ */
+#ifndef MVB200_H
+#define MVB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MVB_API __attribute__((visibility("default")))
+#else
+#define MVB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MVB_OK 0
+#define MVB_ERR_INVALID_ARGUMENT (-1)   /* null pointer, negative size, bad stride   */
+#define MVB_ERR_UNSUPPORTED_DTYPE (-2)  /* dtype not supported by this entry point  */
+#define MVB_ERR_UNSUPPORTED_SHAPE (-3)  /* head ratio / head_dim outside the limits */
+#define MVB_ERR_WORKSPACE_TOO_SMALL (-4)
+#define MVB_ERR_CUDA (-5)               /* a CUDA call failed; see mvb_last_cuda_error */
+
+/* Element types. */
+#define MVB_DTYPE_F16 0
+#define MVB_DTYPE_BF16 1
+#define MVB_DTYPE_F32 2
+
+/* Bits OR-ed into the optional device status word by the kernels. */
+#define MVB_STATUS_SLOT_OUT_OF_RANGE 1   /* slot >= num_blocks*block_size: row skipped  */
+#define MVB_STATUS_BLOCK_OUT_OF_RANGE 2  /* block id outside [0,num_blocks): key hidden */
+
+/* Library version, (major << 16) | minor. */
+MVB_API int mvb_version(void);
+
+/* Human-readable name of a status code. */
+MVB_API const char* mvb_status_string(int status);
+
+/* cudaError_t of the last failed CUDA call on this host thread (0 if none). */
+MVB_API int mvb_last_cuda_error(void);
+
+/*
+ * KV-cache scatter ("reshape_and_cache").
+ *
+ * Replaces write_kv_cache (src/micro_vllm/attention/operators/reference.py:84-98)
+ * and triton_write_kv_cache / _write_kv_cache_kernel
+ * (src/micro_vllm/attention/operators/triton_paged.py:293-325, :11-68).
+ *
+ * For every token t and KV head h, copies key[t,h,:] to
+ * kv_cache[0, s / block_size, s % block_size, h, :] and value[t,h,:] to
+ * plane 1, where s = slot_mapping[t].  The copy is bit-exact.  A negative
+ * slot writes nothing (CUDA-graph padding); a slot past the pool writes
+ * nothing and sets MVB_STATUS_SLOT_OUT_OF_RANGE in *status when status is
+ * not NULL.  key_strides / value_strides are element strides of
+ * [token, head, dim] (host arrays of 3).  dtype is any MVB_DTYPE_*.
+ */
+MVB_API int mvb_reshape_and_cache(const void* key, const int64_t* key_strides, const void* value,
+                          const int64_t* value_strides, void* kv_cache, int64_t num_blocks,
+                          int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                          const int64_t* slot_mapping, int64_t num_tokens, int32_t dtype,
+                          int32_t* status, void* stream);
+
+/*
+ * Bytes of device workspace mvb_paged_attention needs for batches of at
+ * most max_num_tokens query tokens and max_num_requests requests.  The
+ * workspace must be 256-byte aligned; its contents need no initialisation
+ * and are owned by the library between calls on the same stream.
+ */
+MVB_API size_t mvb_paged_attention_workspace_size(int64_t max_num_tokens, int64_t max_num_requests,
+                                          int32_t num_q_heads, int32_t num_kv_heads,
+                                          int32_t head_dim);
+
+/*
+ * Paged attention over the cache (no cache write).
+ *
+ * Replaces the attention part of ReferenceAttentionOperator.forward
+ * (src/micro_vllm/attention/operators/reference.py:26-81, with
+ * gather_kv_cache :101-138) and triton_paged_attention /
+ * _paged_attention_kernel (src/micro_vllm/attention/operators/triton_paged.py:328-389,
+ * :97-290).
+ *
+ * Query token t of request r (query_start_locations[r] <= t <
+ * query_start_locations[r+1]) attends to the logical key positions
+ *   max(ctx_start[first token of r], ctx_start[t]) .. min(context_lengths[r]-1, pos[t])
+ * read through block_table[r, p / block_size]; query head j uses KV head
+ * j / (num_q_heads / num_kv_heads); weights are softmax(q.k * scale) in
+ * fp32.  Rows of tokens owned by no request are written as 0.  fp16 and
+ * bf16 run the tensor-core kernels; fp32 runs the exact CUDA-core kernel.
+ */
+MVB_API int mvb_paged_attention(const void* query, int64_t query_token_stride, int64_t query_head_stride,
+                        void* output, const void* kv_cache, int64_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, const int64_t* query_positions,
+                        const int64_t* query_context_starts, const int64_t* query_start_locations,
+                        const int64_t* context_lengths, const int64_t* block_table,
+                        int64_t block_table_row_stride, int64_t block_table_width,
+                        int64_t num_tokens, int64_t num_requests, int32_t num_q_heads, float scale,
+                        int32_t dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+                        void* stream);
+
+/*
+ * One AttentionOperator.forward: mvb_reshape_and_cache of key/value at
+ * slot_mapping, then mvb_paged_attention, on the same stream.
+ *
+ * Replaces AttentionOperator.forward (src/micro_vllm/attention/operators/base.py:30-40)
+ * as implemented by ReferenceAttentionOperator (reference.py:14-81) and
+ * TritonPagedAttentionOperator (triton_paged.py:392-418).
+ */
+MVB_API int mvb_attention_forward(const void* query, int64_t query_token_stride, int64_t query_head_stride,
+                          const void* key, const int64_t* key_strides, const void* value,
+                          const int64_t* value_strides, void* output, void* kv_cache,
+                          int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                          int32_t head_dim, const int64_t* query_positions,
+                          const int64_t* query_context_starts, const int64_t* query_start_locations,
+                          const int64_t* context_lengths, const int64_t* block_table,
+                          int64_t block_table_row_stride, int64_t block_table_width,
+                          const int64_t* slot_mapping, int64_t num_tokens, int64_t num_requests,
+                          int32_t num_q_heads, float scale, int32_t dtype, void* workspace,
+                          size_t workspace_bytes, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MVB200_H */

@@ -1,0 +1,39 @@
+"""B200 (sm_100a) paged-attention backend for micro-vLLM.
+
+The hot path of micro-vLLM's attention-operator layer — the KV-cache scatter
+and paged attention over that cache — as hand-written CUDA behind a C ABI
+(include/mvb200.h, ``libmvb200.so``), with a Python operator that mirrors
+the reference's ``AttentionOperator`` interface.
+"""
+
+from micro_vllm_b200.attention import (  # noqa: F401
+    Attention,
+    AttentionMetadata,
+    AttentionSpec,
+    ChunkedLocalSpec,
+    FullAttentionSpec,
+    SlidingWindowSpec,
+    map_cache_slots,
+)
+from micro_vllm_b200.operators import (  # noqa: F401
+    OPERATOR_NAME,
+    AttentionOperator,
+    B200PagedAttentionOperator,
+    get_attention_operator_class,
+    write_kv_cache,
+)
+
+__all__ = [
+    "Attention",
+    "AttentionMetadata",
+    "AttentionOperator",
+    "AttentionSpec",
+    "B200PagedAttentionOperator",
+    "ChunkedLocalSpec",
+    "FullAttentionSpec",
+    "OPERATOR_NAME",
+    "SlidingWindowSpec",
+    "get_attention_operator_class",
+    "map_cache_slots",
+    "write_kv_cache",
+]

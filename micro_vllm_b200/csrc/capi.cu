@@ -1,0 +1,164 @@
+// extern "C" entry points declared in include/mvb200.h: argument checks,
+// dtype/shape dispatch and error reporting.  No entry point allocates,
+// synchronises or reads device memory from the host.
+#include <stdio.h>
+
+#include "mvb_common.cuh"
+#include "mvb_internal.h"
+
+namespace mvb {
+
+namespace {
+thread_local int g_last_cuda_error = 0;
+}
+
+void set_last_cuda_error(cudaError_t err) { g_last_cuda_error = (int)err; }
+
+int check_launch() {
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    set_last_cuda_error(err);
+    return MVB_ERR_CUDA;
+  }
+  return MVB_OK;
+}
+
+int elem_bytes_of(int32_t dtype) {
+  switch (dtype) {
+    case MVB_DTYPE_F16:
+    case MVB_DTYPE_BF16:
+      return 2;
+    case MVB_DTYPE_F32:
+      return 4;
+    default:
+      return 0;
+  }
+}
+
+}  // namespace mvb
+
+using namespace mvb;
+
+extern "C" {
+
+int mvb_version(void) { return (0 << 16) | 1; }
+
+const char* mvb_status_string(int status) {
+  switch (status) {
+    case MVB_OK:
+      return "ok";
+    case MVB_ERR_INVALID_ARGUMENT:
+      return "invalid argument";
+    case MVB_ERR_UNSUPPORTED_DTYPE:
+      return "unsupported dtype";
+    case MVB_ERR_UNSUPPORTED_SHAPE:
+      return "unsupported shape";
+    case MVB_ERR_WORKSPACE_TOO_SMALL:
+      return "workspace too small";
+    case MVB_ERR_CUDA:
+      return "CUDA error";
+    default:
+      return "unknown status";
+  }
+}
+
+int mvb_last_cuda_error(void) { return g_last_cuda_error; }
+
+int mvb_reshape_and_cache(const void* key, const int64_t* key_strides, const void* value,
+                          const int64_t* value_strides, void* kv_cache, int64_t num_blocks,
+                          int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                          const int64_t* slot_mapping, int64_t num_tokens, int32_t dtype,
+                          int32_t* status, void* stream) {
+  const int eb = elem_bytes_of(dtype);
+  if (eb == 0) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens < 0 || num_blocks < 0 || block_size <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MVB_OK;
+  if (!key || !value || !kv_cache || !slot_mapping || !key_strides || !value_strides)
+    return MVB_ERR_INVALID_ARGUMENT;
+  return launch_reshape_and_cache(key, key_strides, value, value_strides, kv_cache, num_blocks,
+                                  block_size, num_kv_heads, head_dim, slot_mapping, num_tokens, eb,
+                                  status, static_cast<cudaStream_t>(stream));
+}
+
+size_t mvb_paged_attention_workspace_size(int64_t max_num_tokens, int64_t max_num_requests,
+                                          int32_t num_q_heads, int32_t num_kv_heads,
+                                          int32_t head_dim) {
+  if (max_num_tokens < 0 || max_num_requests < 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      head_dim <= 0)
+    return 0;
+  return workspace_bytes_for(max_num_tokens, max_num_requests, num_q_heads, num_kv_heads,
+                             head_dim);
+}
+
+int mvb_paged_attention(const void* query, int64_t query_token_stride, int64_t query_head_stride,
+                        void* output, const void* kv_cache, int64_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, const int64_t* query_positions,
+                        const int64_t* query_context_starts, const int64_t* query_start_locations,
+                        const int64_t* context_lengths, const int64_t* block_table,
+                        int64_t block_table_row_stride, int64_t block_table_width,
+                        int64_t num_tokens, int64_t num_requests, int32_t num_q_heads, float scale,
+                        int32_t dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+                        void* stream) {
+  if (elem_bytes_of(dtype) == 0) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens < 0 || num_requests < 0 || num_blocks < 0 || block_size <= 0 ||
+      num_kv_heads <= 0 || head_dim <= 0 || num_q_heads <= 0 || block_table_width < 0)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_q_heads % num_kv_heads != 0) return MVB_ERR_UNSUPPORTED_SHAPE;
+  if (num_tokens == 0) return MVB_OK;
+  if (!query || !output || !kv_cache || !query_positions || !query_context_starts ||
+      !query_start_locations || (num_requests > 0 && (!context_lengths || !block_table)))
+    return MVB_ERR_INVALID_ARGUMENT;
+  AttentionProblem p;
+  p.query = query;
+  p.q_st = query_token_stride;
+  p.q_sh = query_head_stride;
+  p.out = output;
+  p.cache = kv_cache;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.num_kv_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.qpos = query_positions;
+  p.qstart = query_context_starts;
+  p.qsl = query_start_locations;
+  p.ctx_len = context_lengths;
+  p.table = block_table;
+  p.table_stride = block_table_row_stride;
+  p.table_width = block_table_width;
+  p.num_tokens = num_tokens;
+  p.num_requests = num_requests;
+  p.num_q_heads = num_q_heads;
+  p.scale = scale;
+  p.dtype = dtype;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace_bytes;
+  p.status = status;
+  p.stream = static_cast<cudaStream_t>(stream);
+  return run_paged_attention(p);
+}
+
+int mvb_attention_forward(const void* query, int64_t query_token_stride, int64_t query_head_stride,
+                          const void* key, const int64_t* key_strides, const void* value,
+                          const int64_t* value_strides, void* output, void* kv_cache,
+                          int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                          int32_t head_dim, const int64_t* query_positions,
+                          const int64_t* query_context_starts, const int64_t* query_start_locations,
+                          const int64_t* context_lengths, const int64_t* block_table,
+                          int64_t block_table_row_stride, int64_t block_table_width,
+                          const int64_t* slot_mapping, int64_t num_tokens, int64_t num_requests,
+                          int32_t num_q_heads, float scale, int32_t dtype, void* workspace,
+                          size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = mvb_reshape_and_cache(key, key_strides, value, value_strides, kv_cache, num_blocks,
+                                 block_size, num_kv_heads, head_dim, slot_mapping, num_tokens,
+                                 dtype, status, stream);
+  if (rc != MVB_OK) return rc;
+  return mvb_paged_attention(query, query_token_stride, query_head_stride, output, kv_cache,
+                             num_blocks, block_size, num_kv_heads, head_dim, query_positions,
+                             query_context_starts, query_start_locations, context_lengths,
+                             block_table, block_table_row_stride, block_table_width, num_tokens,
+                             num_requests, num_q_heads, scale, dtype, workspace, workspace_bytes,
+                             status, stream);
+}
+
+}  // extern "C"

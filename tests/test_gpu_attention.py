@@ -1,0 +1,289 @@
+"""Parity of the CUDA path with the oracle and the reference's golden vectors.
+
+Everything here goes through the C ABI (``libmvb200.so``) via the
+``b200_paged`` operator.  Tolerances (from the build's contract):
+  * KV-cache scatter: bit-exact;
+  * fp16 / bf16 attention: |out - ref| <= 2e-3 + 1e-2 * |ref| against an
+    fp32 reference computed on the same (rounded) inputs;
+  * fp32 attention (exact CUDA-core kernel): 1e-5.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _golden import cache_digest, case_names, load_case
+from _oracle_bridge import assert_close, oracle_subset, snapshot_pages
+from micro_vllm_b200 import AttentionMetadata, B200PagedAttentionOperator, write_kv_cache
+from micro_vllm_b200 import _lib
+from micro_vllm_b200.workloads import paged_batch, uniform_lengths
+from oracle import OracleMetadata, paged_attention, write_kv_cache as oracle_write
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+DEV = torch.device("cuda", 0)
+
+
+def _case_on_device(case: dict, dtype: torch.dtype):
+    t = lambda name: torch.from_numpy(np.ascontiguousarray(case[name]))  # noqa: E731
+    md = AttentionMetadata(
+        query_positions=t("query_positions").to(DEV),
+        query_context_start_positions=t("query_context_start_positions").to(DEV),
+        query_start_locations=t("query_start_locations").to(DEV),
+        context_lengths=t("context_lengths").to(DEV),
+        block_table=t("block_table").to(DEV),
+        slot_mapping=t("slot_mapping").to(DEV),
+        block_size=case["block_size"],
+    )
+    conv = lambda name: torch.from_numpy(case[name].astype(np.float32)).to(DEV, dtype)  # noqa: E731
+    return conv("query"), conv("key"), conv("value"), conv("cache_before"), md
+
+
+def _oracle_md(case: dict) -> OracleMetadata:
+    return OracleMetadata(
+        query_positions=case["query_positions"],
+        query_context_start_positions=case["query_context_start_positions"],
+        query_start_locations=case["query_start_locations"],
+        context_lengths=case["context_lengths"],
+        block_table=case["block_table"],
+        slot_mapping=case["slot_mapping"],
+        block_size=case["block_size"],
+    )
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_golden_fp16_matches_reference(name: str) -> None:
+    """fp16 inputs equal the fixture's exactly; compare to the reference's
+    fp32 output, and the written cache bit-for-bit to the reference's."""
+
+    case = load_case(name)
+    q, k, v, cache, md = _case_on_device(case, torch.float16)
+    out = B200PagedAttentionOperator()(q, k, v, cache, md)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out.shape == q.shape
+    assert_close(out, case["expected_output"], ATOL, RTOL)
+    assert cache_digest(cache.float().cpu().numpy()) == case["expected_cache_sha256"]
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_golden_fp32_matches_reference_tightly(name: str) -> None:
+    case = load_case(name)
+    q, k, v, cache, md = _case_on_device(case, torch.float32)
+    out = B200PagedAttentionOperator()(q, k, v, cache, md)
+    torch.cuda.synchronize()
+    assert_close(out, case["expected_output"], 1e-5, 1e-5)
+    assert cache_digest(cache.cpu().numpy()) == case["expected_cache_sha256"]
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_golden_bf16_matches_oracle(name: str) -> None:
+    case = load_case(name)
+    q, k, v, cache, md = _case_on_device(case, torch.bfloat16)
+    # The oracle sees exactly the bf16-rounded values the kernel sees.
+    qn, kn, vn, cn = (x.float().cpu().numpy() for x in (q, k, v, cache))
+    expected = paged_attention(qn, kn, vn, cn, _oracle_md(case))
+    out = B200PagedAttentionOperator()(q, k, v, cache, md)
+    torch.cuda.synchronize()
+    assert_close(out, expected, ATOL, RTOL)
+    assert np.array_equal(cache.float().cpu().numpy(), cn, equal_nan=True)
+
+
+def _run_and_check(batch, rows=None, atol=ATOL, rtol=RTOL, op=None):
+    rows = list(range(batch.num_requests)) if rows is None else rows
+    snap = snapshot_pages(batch.cache, batch.metadata.block_table, batch.context_lengths, rows)
+    op = op or B200PagedAttentionOperator()
+    out = op(batch.query, batch.key, batch.value, batch.cache, batch.metadata)
+    torch.cuda.synchronize()
+    expected, tok = oracle_subset(batch, rows, snap)
+    assert_close(out[torch.tensor(tok, device=DEV)], expected, atol, rtol)
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("num_q_heads,num_kv_heads", [(16, 8), (32, 8), (8, 8), (64, 8), (14, 2)])
+def test_decode_batch_matches_oracle(dtype, num_q_heads, num_kv_heads) -> None:
+    """Split-KV decode with long and short contexts (many splits, merges)."""
+
+    ctx = uniform_lengths(24, 1, 3000, seed=num_q_heads) + [1, 16, 17, 4096]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=[1] * len(ctx), num_q_heads=num_q_heads,
+        num_kv_heads=num_kv_heads, head_dim=128, block_size=16, num_blocks=20000,
+        dtype=dtype, device=DEV, seed=7,
+    )
+    _run_and_check(batch)
+
+
+@pytest.mark.parametrize("block_size", [1, 5, 8, 32, 64])
+def test_decode_any_block_size(block_size: int) -> None:
+    ctx = uniform_lengths(12, 1, 700, seed=block_size)
+    nb = sum(-(-c // block_size) for c in ctx) + 50
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=[1] * len(ctx), num_q_heads=16, num_kv_heads=8,
+        head_dim=128, block_size=block_size, num_blocks=nb, dtype=torch.float16, device=DEV, seed=3,
+    )
+    _run_and_check(batch)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_mixed_prefill_and_decode_batch(dtype) -> None:
+    """Chunked prefill over cached prefixes (prefix-cache hits), short
+    multi-token chunks that still fit the decode tile, and decodes."""
+
+    ctx = [2048 + 300, 700, 40, 1500, 5, 999, 64, 129]
+    qlen = [2048, 1, 4, 3, 5, 1, 64, 2]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=4000, dtype=dtype, device=DEV, seed=11,
+    )
+    _run_and_check(batch)
+
+
+@pytest.mark.parametrize("window", [1, 7, 40, 600])
+def test_sliding_window_decode_and_chunks(window: int) -> None:
+    ctx = [1000, 37, 600, 2500, 3]
+    qlen = [1, 4, 1, 33, 3]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=2000, dtype=torch.float16, device=DEV, seed=window, window=window,
+    )
+    _run_and_check(batch)
+
+
+def test_graph_padding_rows_are_zero_and_cache_untouched() -> None:
+    """test_triton_paged.py:180-247 at the production head shape: a
+    zero-length request, slot -1 and tokens owned by no request."""
+
+    bs, nb = 16, 40
+    cache = torch.full((2, nb, bs, 8, 128), float("nan"), dtype=torch.float16, device=DEV)
+    q = torch.randn((6, 16, 128), dtype=torch.float16, device=DEV)
+    k = torch.randn((6, 8, 128), dtype=torch.float16, device=DEV)
+    v = torch.randn((6, 8, 128), dtype=torch.float16, device=DEV)
+    table = torch.tensor([[7, 3, 39], [39, 39, 39], [39, 39, 39]], device=DEV)
+    md = AttentionMetadata(
+        query_positions=torch.tensor([0, 1, 2, 0, 0, 0], device=DEV),
+        query_context_start_positions=torch.zeros(6, dtype=torch.int64, device=DEV),
+        query_start_locations=torch.tensor([0, 3, 3, 3], device=DEV),
+        context_lengths=torch.tensor([3, 0, 0], device=DEV),
+        block_table=table,
+        slot_mapping=torch.tensor([112, 113, 114, -1, -1, -1], device=DEV),
+        block_size=bs,
+    )
+    before = cache.clone()
+    out = B200PagedAttentionOperator()(q, k, v, cache, md)
+    torch.cuda.synchronize()
+    assert torch.all(out[3:] == 0)
+    changed = ~(torch.isnan(before) & torch.isnan(cache)) & (before != cache)
+    assert changed.view(2, -1, 8, 128)[:, [112, 113, 114]].all()
+    changed.view(2, -1, 8, 128)[:, [112, 113, 114]] = False
+    assert not changed.any()
+    qn, kn, vn = (x[:3].float().cpu().numpy() for x in (q, k, v))
+    cn = np.full((2, nb, bs, 8, 128), np.nan, np.float32)
+    omd = OracleMetadata(
+        query_positions=np.array([0, 1, 2]), query_context_start_positions=np.zeros(3, np.int64),
+        query_start_locations=np.array([0, 3]), context_lengths=np.array([3]),
+        block_table=np.array([[7, 3, 39]]), slot_mapping=np.array([112, 113, 114]), block_size=bs,
+    )
+    assert_close(out[:3], paged_attention(qn, kn, vn, cn, omd, out_dtype=np.float32), ATOL, RTOL)
+
+
+def test_out_of_range_block_ids_are_never_read() -> None:
+    """A block id past the pool is excluded (and reported) instead of read."""
+
+    bs, nb = 16, 8
+    cache = torch.randn((2, nb, bs, 8, 128), dtype=torch.float16, device=DEV)
+    q = torch.randn((1, 16, 128), dtype=torch.float16, device=DEV)
+    kv = torch.randn((1, 8, 128), dtype=torch.float16, device=DEV)
+    md = AttentionMetadata(
+        query_positions=torch.tensor([40], device=DEV),
+        query_context_start_positions=torch.zeros(1, dtype=torch.int64, device=DEV),
+        query_start_locations=torch.tensor([0, 1], device=DEV),
+        context_lengths=torch.tensor([41], device=DEV),
+        block_table=torch.tensor([[2, 1 << 40, 5]], device=DEV),
+        slot_mapping=torch.tensor([5 * bs + 8], device=DEV),
+        block_size=bs,
+    )
+    op = B200PagedAttentionOperator()
+    out = op(q, kv, kv, cache, md)
+    assert op.read_status(DEV) & _lib.MVB_STATUS_BLOCK_OUT_OF_RANGE
+    assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("head_dim", [7, 64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_kv_write_is_bit_exact_for_strided_inputs(head_dim: int, dtype) -> None:
+    """tests/benchmarks/test_spike_triton_paged.py:84-129: key is a strided
+    view (every other element), slots cross pages, -1 is skipped."""
+
+    bs, nb, hkv = 4, 6, 3
+    storage = torch.randn((5, hkv, head_dim * 2), device=DEV).to(dtype)
+    key = storage[..., ::2]
+    value = torch.randn((5, hkv, head_dim), device=DEV).to(dtype)
+    slots = torch.tensor([7, 2, -1, 8, 23], device=DEV)
+    cache = torch.randn((2, nb, bs, hkv, head_dim), device=DEV).to(dtype)
+    expected = cache.float().cpu().numpy().copy()
+    oracle_write(key.float().cpu().numpy(), value.float().cpu().numpy(), expected, slots.cpu().numpy())
+    md = AttentionMetadata(
+        query_positions=torch.zeros(5, dtype=torch.int64, device=DEV),
+        query_context_start_positions=torch.zeros(5, dtype=torch.int64, device=DEV),
+        query_start_locations=torch.tensor([0, 5], device=DEV),
+        context_lengths=torch.tensor([1], device=DEV),
+        block_table=torch.zeros((1, 1), dtype=torch.int64, device=DEV),
+        slot_mapping=slots,
+        block_size=bs,
+    )
+    write_kv_cache(key, value, cache, md)
+    torch.cuda.synchronize()
+    assert np.array_equal(cache.float().cpu().numpy(), expected)
+
+
+def test_kv_write_at_decode_scale_is_bit_exact() -> None:
+    """256 tokens x 8 heads x 128 scattered over a 20k-page pool."""
+
+    bs, nb = 16, 20000
+    gen = torch.Generator().manual_seed(5)
+    slots = torch.randperm(nb * bs, generator=gen)[:256].to(DEV)
+    key = torch.randn((256, 8, 128), device=DEV, dtype=torch.float16)
+    value = torch.randn((256, 8, 128), device=DEV, dtype=torch.float16)
+    cache = torch.zeros((2, nb, bs, 8, 128), device=DEV, dtype=torch.float16)
+    md = AttentionMetadata(
+        query_positions=torch.zeros(256, dtype=torch.int64, device=DEV),
+        query_context_start_positions=torch.zeros(256, dtype=torch.int64, device=DEV),
+        query_start_locations=torch.tensor([0, 256], device=DEV),
+        context_lengths=torch.tensor([1], device=DEV),
+        block_table=torch.zeros((1, 1), dtype=torch.int64, device=DEV),
+        slot_mapping=slots,
+        block_size=bs,
+    )
+    write_kv_cache(key, value, cache, md)
+    flat = cache.view(2, -1, 8, 128)
+    assert torch.equal(flat[0, slots], key) and torch.equal(flat[1, slots], value)
+    assert int((flat != 0).any(dim=(2, 3)).sum()) == 2 * 256
+
+
+def test_physical_placement_does_not_change_the_output() -> None:
+    """Size-independent property at the benchmark's batch shape: the same
+    logical contexts stored in two different page placements give
+    bit-identical outputs (placement only changes addresses)."""
+
+    ctx = uniform_lengths(256, 512, 4096, seed=0)
+    kw = dict(context_lengths=ctx, query_lengths=[1] * 256, num_q_heads=16, num_kv_heads=8,
+              head_dim=128, block_size=16, dtype=torch.float16, device=DEV)
+    a = paged_batch(num_blocks=40000, seed=1, **kw)
+    b = paged_batch(num_blocks=41000, seed=1, fill_cache=False, **kw)
+    # Copy a's logical pages into b's placement.
+    ta, tb = a.metadata.block_table, b.metadata.block_table
+    for r, c in enumerate(ctx):
+        n = -(-c // 16)
+        b.cache[:, tb[r, :n]] = a.cache[:, ta[r, :n]]
+    op = B200PagedAttentionOperator()
+    out_a = op(a.query, a.key, a.value, a.cache, a.metadata)
+    out_b = op(b.query, b.key, b.value, b.cache, b.metadata)
+    torch.cuda.synchronize()
+    assert torch.equal(out_a, out_b)
+    # And a sample of sequences against the oracle at this size.
+    rows = [0, 17, 99, 255]
+    snap_batch = paged_batch(num_blocks=40000, seed=1, **kw)
+    _run_and_check(snap_batch, rows=rows, op=op)

@@ -1,0 +1,283 @@
+"""Pin the CPU oracle before trusting it.
+
+1. Against every golden vector produced by the reference's own
+   ``ReferenceAttentionOperator`` (tests/golden/make_golden.py): outputs
+   within 1e-5 (both are fp32 math; only summation order differs) and the
+   full post-write cache bit-exact (SHA-256 of its fp32 bytes).
+2. Against the known answers in the reference's operator tests
+   (tests/attention/operators/test_reference.py in the reference project),
+   restated here on the oracle.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from _golden import cache_digest, case_names, load_case, oracle_metadata
+from oracle import (
+    OracleMetadata,
+    build_metadata,
+    chunked_local_context_start,
+    gather_kv_cache,
+    paged_attention,
+    sliding_window_context_start,
+    write_kv_cache,
+)
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_oracle_matches_reference_golden_vectors(name: str) -> None:
+    case = load_case(name)
+    cache = case["cache_before"].astype(np.float32)
+    out = paged_attention(
+        case["query"].astype(np.float32),
+        case["key"].astype(np.float32),
+        case["value"].astype(np.float32),
+        cache,
+        oracle_metadata(case),
+    )
+    np.testing.assert_allclose(out, case["expected_output"], atol=1e-5, rtol=1e-5)
+    assert cache_digest(cache) == case["expected_cache_sha256"]
+
+
+def test_oracle_thread_pool_changes_nothing() -> None:
+    case = load_case("mixed_chunked")
+    args = [case[k].astype(np.float32) for k in ("query", "key", "value")]
+    serial = paged_attention(*args, case["cache_before"].astype(np.float32), oracle_metadata(case))
+    threaded = paged_attention(
+        *args, case["cache_before"].astype(np.float32), oracle_metadata(case), num_threads=4
+    )
+    assert np.array_equal(serial, threaded)
+
+
+def _md(**kw) -> OracleMetadata:
+    kw.setdefault("query_context_start_positions", np.zeros_like(kw["query_positions"]))
+    return OracleMetadata(**{k: (np.asarray(v, np.int64) if k != "block_size" else v) for k, v in kw.items()})
+
+
+def test_visibility_start_known_answer() -> None:
+    """test_reference.py:114-139 — keys before the visibility start are
+    hidden; the two visible values 20 and 30 with equal scores give 25."""
+
+    cache = np.zeros((2, 2, 2, 1, 1), np.float32)
+    flat = cache.reshape(2, 4, 1, 1)
+    flat[0, 0], flat[1, 0], flat[0, 1], flat[1, 1] = 1, 100, 1, 20
+    md = _md(
+        query_positions=[2],
+        query_context_start_positions=[1],
+        query_start_locations=[0, 1],
+        context_lengths=[3],
+        block_table=[[0, 1]],
+        slot_mapping=[2],
+        block_size=2,
+    )
+    out = paged_attention(
+        np.ones((1, 1, 1), np.float32),
+        np.ones((1, 1, 1), np.float32),
+        np.full((1, 1, 1), 30.0, np.float32),
+        cache,
+        md,
+    )
+    assert out.shape == (1, 1, 1) and abs(float(out[0, 0, 0]) - 25.0) < 1e-6
+
+
+def test_write_uses_flattened_physical_slots() -> None:
+    """test_reference.py:157-178."""
+
+    cache = np.zeros((2, 2, 4, 2, 2), np.float32)
+    key = np.array([[[1, 2], [3, 4]], [[5, 6], [7, 8]]], np.float32)
+    value = key + 10
+    write_kv_cache(key, value, cache, np.array([1, 6]))
+    flat = cache.reshape(2, 8, 2, 2)
+    assert np.array_equal(flat[0, 1], key[0]) and np.array_equal(flat[0, 6], key[1])
+    assert np.array_equal(flat[1, 1], value[0]) and np.array_equal(flat[1, 6], value[1])
+    assert np.count_nonzero(flat[:, [0, 2, 3, 4, 5, 7]]) == 0
+
+
+def test_write_skips_negative_slots_and_rejects_slots_past_the_pool() -> None:
+    cache = np.full((2, 2, 2, 1, 2), 7.0, np.float32)
+    key = np.ones((2, 1, 2), np.float32)
+    write_kv_cache(key, key + 1, cache, np.array([-1, 3]))
+    flat = cache.reshape(2, 4, 1, 2)
+    assert np.all(flat[:, :3] == 7.0) and np.all(flat[0, 3] == 1) and np.all(flat[1, 3] == 2)
+    with pytest.raises(IndexError):
+        write_kv_cache(key, key, cache, np.array([0, 4]))
+
+
+def test_gather_handles_each_request_independently() -> None:
+    """test_reference.py:202-232."""
+
+    cache = np.full((2, 5, 2, 1, 1), 99.0, np.float32)
+    flat = cache.reshape(2, 10, 1, 1)
+    flat[0, [6, 7, 2, 8], 0, 0] = [10, 11, 12, 20]
+    flat[1, [6, 7, 2, 8], 0, 0] = [110, 111, 112, 120]
+    md = _md(
+        query_positions=[1, 2, 0],
+        query_start_locations=[0, 2, 3],
+        context_lengths=[3, 1],
+        block_table=[[3, 1, 0], [4, 0, 0]],
+        slot_mapping=[7, 2, 8],
+        block_size=2,
+    )
+    hist = gather_kv_cache(cache, md)
+    assert [k.flatten().tolist() for k, _ in hist] == [[10, 11, 12], [20]]
+    assert [v.flatten().tolist() for _, v in hist] == [[110, 111, 112], [120]]
+
+
+def test_gather_reads_only_the_minimum_contiguous_context() -> None:
+    """test_reference.py:298-322: gathering starts at the first query's
+    visibility start."""
+
+    cache = np.zeros((2, 4, 2, 1, 1), np.float32)
+    flat = cache.reshape(2, 8, 1, 1)
+    flat[0, [1, 6, 7], 0, 0] = [3, 4, 5]
+    flat[1, [1, 6, 7], 0, 0] = [13, 14, 15]
+    md = _md(
+        query_positions=[4, 5],
+        query_context_start_positions=[3, 4],
+        query_start_locations=[0, 2],
+        context_lengths=[6],
+        block_table=[[2, 0, 3]],
+        slot_mapping=[6, 7],
+        block_size=2,
+    )
+    ((k, v),) = gather_kv_cache(cache, md)
+    assert k.flatten().tolist() == [3, 4, 5] and v.flatten().tolist() == [13, 14, 15]
+
+
+def dense_attention(q, k, v, positions=None, starts=None) -> np.ndarray:
+    """Dense masked attention over a contiguous history (the reference
+    tests' ``dense_causal_attention``, test_reference.py:325-360)."""
+
+    t, hq, d = q.shape
+    g = hq // k.shape[1]
+    kk = np.repeat(k, g, axis=1).astype(np.float64)
+    vv = np.repeat(v, g, axis=1).astype(np.float64)
+    pos = np.arange(t) if positions is None else np.asarray(positions)
+    st = np.zeros_like(pos) if starts is None else np.asarray(starts)
+    kpos = np.arange(k.shape[0])
+    s = np.einsum("qhd,khd->hqk", q.astype(np.float64), kk) / math.sqrt(d)
+    hidden = (kpos[None, :] < st[:, None]) | (kpos[None, :] > pos[:, None])
+    s = np.where(hidden[None], -np.inf, s)
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    return np.einsum("hqk,khd->qhd", w, vv)
+
+
+def _linspace_tensors(t, hq=4, hkv=2, d=3):
+    """The reference tests' ``make_attention_tensors`` (test_reference.py:428-460)."""
+
+    q = np.linspace(-0.8, 0.9, t * hq * d, dtype=np.float32).reshape(t, hq, d)
+    k = np.linspace(0.7, -0.6, t * hkv * d, dtype=np.float32).reshape(t, hkv, d)
+    v = np.linspace(-1.0, 1.0, t * hkv * d, dtype=np.float32).reshape(t, hkv, d)
+    return q, k, v
+
+
+@pytest.mark.parametrize("hkv", [4, 2, 1])
+def test_full_prefill_matches_dense_mha_gqa_mqa(hkv: int) -> None:
+    """test_reference.py:463-497."""
+
+    q = np.arange(24, dtype=np.float32).reshape(3, 4, 2) / 10
+    k = np.arange(3 * hkv * 2, dtype=np.float32).reshape(3, hkv, 2) / 20
+    v = k + 1
+    cache = np.zeros((2, 3, 2, hkv, 2), np.float32)
+    md = _md(
+        query_positions=[0, 1, 2],
+        query_start_locations=[0, 3],
+        context_lengths=[3],
+        block_table=[[2, 0]],
+        slot_mapping=[4, 5, 0],
+        block_size=2,
+    )
+    out = paged_attention(q, k, v, cache, md)
+    np.testing.assert_allclose(out, dense_attention(q, k, v), atol=1e-6, rtol=1e-6)
+
+
+@pytest.mark.parametrize(
+    "start_fn",
+    [
+        lambda p: sliding_window_context_start(p, 2),
+        lambda p: sliding_window_context_start(p, 6),
+        lambda p: chunked_local_context_start(p, 2),
+        lambda p: chunked_local_context_start(p, 6),
+    ],
+)
+def test_bounded_prefill_matches_dense_mask(start_fn) -> None:
+    """test_reference.py:500-549."""
+
+    q, k, v = _linspace_tensors(9)
+    cache = np.zeros((2, 5, 4, 2, 3), np.float32)
+    md = build_metadata([list(range(9))], [[4, 1, 3]], block_size=4, context_start=start_fn)
+    out = paged_attention(q, k, v, cache, md)
+    expected = dense_attention(q, k, v, md.query_positions, md.query_context_start_positions)
+    np.testing.assert_allclose(out, expected, atol=1e-6, rtol=1e-6)
+
+
+def test_low_precision_dtype_is_restored() -> None:
+    """test_reference.py:552-575."""
+
+    q = np.array([[[1.0, 2.0]]], np.float16)
+    k = np.array([[[2.0, 1.0]]], np.float16)
+    v = np.array([[[3.0, 4.0]]], np.float16)
+    cache = np.zeros((2, 1, 2, 1, 2), np.float16)
+    md = _md(
+        query_positions=[0], query_start_locations=[0, 1], context_lengths=[1],
+        block_table=[[0]], slot_mapping=[0], block_size=2,
+    )
+    out = paged_attention(q, k, v, cache, md)
+    assert out.dtype == np.float16 and np.array_equal(out, v)
+
+
+def test_chunked_prefill_and_decode_match_full_prefill() -> None:
+    """test_reference.py:607-643 and :695-748."""
+
+    q, k, v = _linspace_tensors(6)
+    table = [4, 1, 3]
+    full = paged_attention(
+        q, k, v, np.zeros((2, 5, 2, 2, 3), np.float32),
+        build_metadata([list(range(6))], [table], block_size=2),
+    )
+    cache = np.zeros((2, 5, 2, 2, 3), np.float32)
+    pieces = [
+        paged_attention(q[s:e], k[s:e], v[s:e], cache, build_metadata([list(range(s, e))], [table], block_size=2))
+        for s, e in ((0, 3), (3, 4), (4, 5), (5, 6))
+    ]
+    expected = dense_attention(q, k, v)
+    np.testing.assert_allclose(full, expected, atol=1e-6, rtol=1e-6)
+    np.testing.assert_allclose(np.concatenate(pieces), expected, atol=1e-6, rtol=1e-6)
+
+
+def test_shared_prefix_gives_identical_attention() -> None:
+    """test_reference.py:923-968."""
+
+    pq, pk, pv = _linspace_tensors(2, hq=2, hkv=1)
+    cache = np.zeros((2, 3, 2, 1, 3), np.float32)
+    paged_attention(pq, pk, pv, cache, build_metadata([[0, 1]], [[0]], block_size=2))
+    q, k, v = _linspace_tensors(1, hq=2, hkv=1)
+    q, k, v = q + 0.25, k - 0.15, v + 0.35
+    out = paged_attention(
+        np.concatenate((q, q)), np.concatenate((k, k)), np.concatenate((v, v)), cache,
+        build_metadata([[2], [2]], [[0, 1], [0, 2]], block_size=2),
+    )
+    expected = dense_attention(np.concatenate((pq, q)), np.concatenate((pk, k)), np.concatenate((pv, v)))[-1]
+    np.testing.assert_allclose(out[0], expected, atol=1e-6, rtol=1e-6)
+    np.testing.assert_allclose(out[1], expected, atol=1e-6, rtol=1e-6)
+
+
+def test_padding_rows_are_zero_and_empty_visibility_is_nan() -> None:
+    cache = np.zeros((2, 2, 2, 1, 2), np.float32)
+    q = np.ones((3, 1, 2), np.float32)
+    md = _md(
+        query_positions=[0, 1, 0],
+        query_context_start_positions=[0, 5, 0],  # token 1 sees nothing
+        query_start_locations=[0, 2, 2],
+        context_lengths=[2, 0],
+        block_table=[[0, 1], [1, 1]],
+        slot_mapping=[0, 1, -1],
+        block_size=2,
+    )
+    out = paged_attention(q, q, q, cache, md)
+    assert np.all(np.isfinite(out[0])) and np.all(np.isnan(out[1])) and np.all(out[2] == 0)
