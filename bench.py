@@ -54,6 +54,9 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--ctx", choices=("uniform", "fixed4096"), default="uniform")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--pool-gb", type=float, default=None,
+                    help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
     return ap.parse_args()
 
 
@@ -245,7 +248,10 @@ def run_ours(args) -> None:
     elsize = 2
 
     ctx = context_lengths(args.ctx, BATCH_PER_GPU, seed=1000 + rank)
-    nb = pool_blocks_for_fraction(POOL_FRACTION, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, dtype, dev)
+    if args.pool_gb is None:
+        nb = pool_blocks_for_fraction(POOL_FRACTION, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, dtype, dev)
+    else:
+        nb = int(args.pool_gb * 1e9) // (2 * BLOCK_SIZE * NUM_KV_HEADS * HEAD_DIM * elsize)
     batch = paged_batch(
         context_lengths=ctx, query_lengths=[1] * BATCH_PER_GPU, num_q_heads=NUM_Q_HEADS,
         num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE, num_blocks=nb,
@@ -339,16 +345,18 @@ def run_ours(args) -> None:
         out = op(d["q"], d["k"], d["v"], batch.cache, emd)
         out_host.copy_(out, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e_stop.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.steps)
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        for _ in range(3):
+            e2e_step()
+        barrier()
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e_stop.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.steps)
 
     attn_bytes = decode_bytes(ctx, elsize)
     step_bytes_all = attn_bytes * world  # every rank runs the same-size workload

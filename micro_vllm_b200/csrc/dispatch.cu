@@ -1,7 +1,5 @@
 // run_paged_attention: picks the kernels for one call and carves the
 // caller's workspace.  Nothing here touches device memory from the host.
-#include <stdlib.h>
-
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
 
@@ -11,34 +9,29 @@ namespace {
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-int env_int(const char* name, int fallback) {
-  const char* v = getenv(name);
-  if (v == nullptr || *v == '\0') return fallback;
-  const int x = atoi(v);
-  return x > 0 ? x : fallback;
-}
-
 }  // namespace
 
-WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads, int32_t head_dim,
-                                 size_t workspace_bytes) {
+WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads) {
   WorkspaceLayout w;
   size_t off = 0;
   w.ctrl = off;
-  off += align256(kCtrlWords * sizeof(int32_t));
-  w.unit_prefix = off;
-  off += align256((size_t)(num_requests + 1) * sizeof(int32_t));
+  off += align256(kCtrlWords * sizeof(int64_t));
+  w.tile_prefix = off;
+  off += align256((size_t)(num_requests + 1) * sizeof(int64_t));
+  w.cta_start = off;
+  off += align256((size_t)kMaxDecodeCtas * sizeof(int32_t));
   w.kind = off;
   off += align256((size_t)num_requests * sizeof(int32_t));
   w.merge_count = off;
   off += align256((size_t)num_requests * num_kv_heads * sizeof(int32_t));
-  w.end_fixed = off;
-  w.item_bytes = (size_t)kDecodeCols * ((size_t)head_dim * sizeof(float) + sizeof(float2));
-  const size_t room = workspace_bytes > off + 256 ? workspace_bytes - off - 256 : 0;
-  w.unit_cap = (int64_t)(room / (w.item_bytes * num_kv_heads));
+  w.zero_row = off;
+  off += align256((size_t)kMaxHeadsPerCta * kDecodeHeadDim * 2);
+  const size_t partials = (size_t)kMaxDecodeCtas * 2 * kMaxHeadsPerCta * kDecodeCols;
   w.partial_ml = off;
-  w.partial_o =
-      off + align256((size_t)w.unit_cap * num_kv_heads * kDecodeCols * sizeof(float2));
+  off += align256(partials * sizeof(float2));
+  w.partial_o = off;
+  off += align256(partials * kDecodeHeadDim * sizeof(float));
+  w.end = off;
   return w;
 }
 
@@ -46,17 +39,8 @@ size_t workspace_bytes_for(int64_t max_tokens, int64_t max_requests, int32_t num
                            int32_t num_kv_heads, int32_t head_dim) {
   (void)max_tokens;
   (void)num_q_heads;
-  const WorkspaceLayout w = workspace_layout(max_requests, num_kv_heads, head_dim, 0);
-  return w.end_fixed + 512 + (size_t)(max_requests + kExtraUnits) * num_kv_heads * w.item_bytes;
-}
-
-PlanTuning plan_tuning() {
-  static const PlanTuning t = {
-      env_int("MVB_DECODE_TARGET_ITEMS", 4096),
-      (env_int("MVB_DECODE_MIN_CHUNK", 64) + 15) & ~15,
-      (env_int("MVB_DECODE_MAX_CHUNK", 1024) + 15) & ~15,
-  };
-  return t;
+  (void)head_dim;
+  return workspace_layout(max_requests, num_kv_heads).end;
 }
 
 int num_sms() {
@@ -84,13 +68,15 @@ int run_paged_attention(const AttentionProblem& p) {
 
   if (p.workspace == nullptr || ((uintptr_t)p.workspace % 256) != 0)
     return MVB_ERR_INVALID_ARGUMENT;
-  const WorkspaceLayout w =
-      workspace_layout(p.num_requests, p.num_kv_heads, p.head_dim, p.workspace_bytes);
-  if (w.unit_cap < p.num_requests + 1) return MVB_ERR_WORKSPACE_TOO_SMALL;
+  const WorkspaceLayout w = workspace_layout(p.num_requests, p.num_kv_heads);
+  if (p.workspace_bytes < w.end) return MVB_ERR_WORKSPACE_TOO_SMALL;
+  int smem = 0;
+  const int grid = decode_grid(p, &smem);
+  if (grid <= 0) return MVB_ERR_CUDA;
 
-  int rc = launch_plan(p, w, group, plan_tuning());
+  int rc = launch_plan(p, w, group, grid);
   if (rc != MVB_OK) return rc;
-  rc = launch_paged_decode(p, w);
+  rc = launch_paged_decode(p, w, grid, smem);
   if (rc != MVB_OK) return rc;
   // Requests whose query chunk does not fit the decode tile.
   const int32_t* kind = reinterpret_cast<const int32_t*>(static_cast<char*>(p.workspace) + w.kind);

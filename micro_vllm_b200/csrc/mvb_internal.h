@@ -30,8 +30,8 @@ struct AttentionProblem {
 
 // Request classes written by the planner (one int32 per request).
 enum RequestKind : int32_t {
-  kKindNone = 0,     // owns no query token
-  kKindDecode = 1,   // query_len * group <= kDecodeCols: split-KV decode kernel
+  kKindNone = 0,     // owns no query token (or malformed)
+  kKindDecode = 1,   // query_len * group <= kDecodeCols: decode kernel
   kKindPrefill = 2,  // longer chunks: prefill kernel
 };
 
@@ -39,31 +39,29 @@ enum RequestKind : int32_t {
 // GQA group): the N dimension of its m16n8k16 tiles.
 constexpr int kDecodeCols = 8;
 constexpr int kDecodeHeadDim = 128;
+// KV heads one decode CTA streams together (a whole 2 KiB token row for
+// 8 heads of 128 fp16/bf16 elements).
+constexpr int kMaxHeadsPerCta = 8;
+// Upper bound on decode CTAs (one or two per SM); sizes the partial area.
+constexpr int kMaxDecodeCtas = 320;
+// Longest context a request may have (2^30 tokens).
+constexpr int64_t kMaxContext = (int64_t)1 << 30;
 
-// Workspace carve-up.  Offsets depend only on (num_requests, num_kv_heads);
-// the remaining bytes hold split-KV partials, one slot per decode item.
-struct WorkspaceLayout {
-  size_t ctrl, unit_prefix, kind, merge_count, partial_ml, partial_o, end_fixed;
-  size_t item_bytes;
-  int64_t unit_cap;  // decode units (request splits) the partial area holds
-};
+// Status bit for a bounded wait that ran out (a kernel bug, never expected).
+constexpr int32_t kStatusWaitTimeout = 4;
 
-// ctrl[] words.
+// ctrl[] words (int64).
 enum CtrlWord : int {
-  kCtrlNumItems = 0,     // decode items = units * num_kv_heads
-  kCtrlCursor = 1,       // persistent decode kernel work cursor
-  kCtrlChunk = 2,        // KV tokens per split (multiple of 16)
-  kCtrlNumUnits = 3,
-  kCtrlPrefillCursor = 4,
-  kCtrlWords = 64,
+  kCtrlTiles = 0,   // decode tiles per KV-head group
+  kCtrlWords = 32,
 };
 
-// Extra decode units beyond one per request that a workspace sized by
-// mvb_paged_attention_workspace_size provides for splitting long contexts.
-constexpr int64_t kExtraUnits = 2048;
+// Workspace carve-up.  Offsets depend only on (num_requests, num_kv_heads).
+struct WorkspaceLayout {
+  size_t ctrl, tile_prefix, cta_start, kind, merge_count, zero_row, partial_ml, partial_o, end;
+};
 
-WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads, int32_t head_dim,
-                                 size_t workspace_bytes);
+WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads);
 size_t workspace_bytes_for(int64_t max_tokens, int64_t max_requests, int32_t num_q_heads,
                            int32_t num_kv_heads, int32_t head_dim);
 
@@ -80,16 +78,15 @@ int launch_reshape_and_cache(const void* key, const int64_t* ks, const void* val
 int launch_paged_attention_generic(const AttentionProblem& p, const int32_t* kind_filter,
                                    int32_t want_kind);
 
-struct PlanTuning {
-  int32_t target_items;  // aim for about this many decode items
-  int32_t min_chunk;     // smallest split in KV tokens (multiple of 16)
-  int32_t max_chunk;     // largest split before capacity forces more
-};
-PlanTuning plan_tuning();
+// Heads a decode CTA streams: the largest divisor of num_kv_heads <= 8.
+int heads_per_cta(int32_t num_kv_heads);
+// Decode grid for this device and problem (also what the planner assumes).
+int decode_grid(const AttentionProblem& p, int* smem_bytes);
 
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,
-                const PlanTuning& tuning);
-int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w);
+                int32_t decode_ctas);
+int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w, int32_t grid,
+                        int32_t smem_bytes);
 
 int num_sms();
 

@@ -1,37 +1,38 @@
-// Split-KV GQA paged decode for head_dim 128, fp16/bf16, on tensor cores.
+// Stream-K split-KV GQA paged decode for head_dim 128, fp16/bf16.
 //
-// Work item = (request, split of its KV positions, KV head), as produced by
-// the device planner (plan.cu).  The kernel is persistent: each 128-thread
-// CTA pulls items from an atomic cursor until none are left.
+// Work decomposition.  The planner lays the KV of every decode-class
+// request out as one sequence of 16-token tiles (per KV-head group of up to
+// 8 heads).  The grid is persistent, one CTA per SM, and CTA b walks the
+// contiguous share [b*N/G, (b+1)*N/G) of the N tiles, so every CTA moves
+// the same number of bytes whatever the context-length mix.  A request
+// whose tiles fall inside one share is finished by that CTA; only requests
+// cut by a share boundary leave fp32 partials (at most two per CTA), which
+// the CTA finishing last merges (an atomic count per request and KV head;
+// no CTA ever waits for another).
 //
-// Inside an item the four warps take 16-token tiles round-robin and run as
-// independent flash-decoding lanes:
-//   * staging: each warp streams its own K and V tiles (16 tokens x 256 B
-//     per plane) into a private STAGES-deep shared-memory ring with 16-byte
-//     cp.async.cg copies, one instruction covering two 256-byte token rows.
-//     Rows are resolved through the block table per tile (one lookup when a
-//     page holds >= 16 tokens).  The 16-byte chunk index is XOR-swizzled by
-//     the row so ldmatrix reads are bank-conflict free.
-//   * scores: S^T = K . Q^T with mma.sync m16n8k16 — the 16 tokens of the
-//     tile are the M dimension and the N = 8 columns hold the queries of
-//     the GQA group (query_len x group <= 8), so one K tile load serves
-//     every query head that shares the KV head.
-//   * softmax: fp32 online softmax per column; the column max is a 3-step
-//     warp shuffle over the 8 lanes holding that column; sums are kept per
-//     lane and reduced once at the end.
-//   * P.V: O^T += V^T . P^T with the probabilities moved from the score
-//     accumulator layout into the B-operand layout by movmatrix.trans.
-// The four warps' (max, sum, O) states are merged through shared memory.
-// A request with one split writes its output directly; otherwise each split
-// stores an fp32 partial (O, max, sum) and the CTA that finishes last (an
-// atomic count per request and KV head — no waiting) merges them.
+// Inside a CTA (warp specialisation, mbarrier ring of kStages tiles):
+//   * producer warp: for each tile, 16 lanes copy the 16 token rows of K
+//     and 16 lanes those of V with cp.async.bulk — each row is the
+//     contiguous heads_per_cta x 256 B piece of one token's cache row, so a
+//     tile moves whole 2 KiB rows (one 32 KiB page per plane at 8 heads).
+//     Rows outside the visible range or with an invalid page are copied
+//     from a zero row, so every tile carries the same byte count.  Rows are
+//     padded by 16 B in shared memory, which makes the ldmatrix reads
+//     below bank-conflict free.
+//   * consumer warps, one per KV head: S^T = K . Q^T with mma.sync
+//     m16n8k16 (16 tokens in M; the 8 N columns hold the query heads of the
+//     GQA group times the request's query tokens), fp32 online softmax with
+//     3-step warp-shuffle column reductions, O^T += V^T . P^T with P moved
+//     into the B-operand layout by movmatrix.trans.
+// Every mbarrier wait is bounded; a wait that runs out sets
+// kStatusWaitTimeout in the status word and the CTA returns.
 //
 // Semantics follow ReferenceAttentionOperator.forward (reference.py:14-81):
 // query token t of request r sees positions
 //   max(ctx_start[first token of r], ctx_start[t]) .. min(ctx_len[r]-1, pos[t]);
 // softmax(q.k * scale) in fp32; empty gathered history -> 0, empty window
-// -> NaN.  HBM traffic per item is one read of its K/V rows: the roofline
-// is HBM bandwidth.
+// -> NaN.  HBM traffic: one read of every visible K/V row (the roofline is
+// HBM bandwidth).
 #include <math.h>
 
 #include "mvb_common.cuh"
@@ -40,13 +41,10 @@
 namespace mvb {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kRowBytes = kDecodeHeadDim * 2;   // one token's head row
-constexpr int kTileTokens = 16;
-constexpr int kTileBytes = kTileTokens * kRowBytes;  // 4 KiB per plane
-constexpr int kStageBytes = 2 * kTileBytes;          // K + V
-constexpr int kColStride = kDecodeHeadDim + 4;       // padded fp32 row in the merge buffer
+constexpr int kTile = 16;
+constexpr int kStages = 3;
+constexpr int kHeadRow = kDecodeHeadDim * 2;  // bytes of one head's row
+constexpr int kWaitLimit = 1 << 22;
 
 struct DecodeParams {
   const char* query;
@@ -55,37 +53,60 @@ struct DecodeParams {
   const char* cache;
   int64_t plane_bytes;
   int64_t num_blocks;
-  int32_t block_size, bs_shift, num_kv_heads, group, num_q_heads;
+  int32_t block_size, bs_shift, num_kv_heads, heads_per_cta, group, num_q_heads;
   const int64_t *qpos, *qstart, *qsl, *ctx_len, *table;
   int64_t table_stride, table_width, num_requests;
   float scale_log2;
-  const int32_t* ctrl;
-  int32_t* cursor;
-  const int32_t* unit_prefix;
+  const int64_t* ctrl;
+  const int64_t* tile_prefix;
+  const int32_t* cta_start;
   int32_t* merge_count;
-  float* partial_o;    // [items][8][128]
-  float2* partial_ml;  // [items][8]  (max, sum)
+  const char* zero_row;
+  float* partial_o;    // [kMaxDecodeCtas][2][8 heads][8 cols][128]
+  float2* partial_ml;  // [kMaxDecodeCtas][2][8 heads][8 cols] (max, sum)
   int32_t* status;
 };
 
+// ------------------------------------------------------------------ PTX
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
-
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool valid) {
-  const int src_size = valid ? 16 : 0;  // 0 = zero-fill, nothing read
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
-               "r"(src_size)
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
-
+// Bounded wait: false (and the status bit) when the barrier never flips.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
+  for (int i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (status != nullptr) atomicOr(status, kStatusWaitTimeout);
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -137,8 +158,9 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Physical block of logical position `pos` of a request, or -1 when the
-// table has no valid entry for it.
+// ------------------------------------------------------------ helpers
+// Physical page of logical position `pos`, or -1 when the table has no
+// valid entry for it.
 __device__ __forceinline__ int64_t page_of(const DecodeParams& p, const int64_t* trow, int64_t pos,
                                            int64_t* offset) {
   int64_t lb;
@@ -149,337 +171,404 @@ __device__ __forceinline__ int64_t page_of(const DecodeParams& p, const int64_t*
     lb = pos / p.block_size;
     *offset = pos - lb * p.block_size;
   }
-  if (lb < 0 || lb >= p.table_width) return -1;
+  if (pos < 0 || lb >= p.table_width) return -1;
   const int64_t blk = __ldg(trow + lb);
   return (blk >= 0 && blk < p.num_blocks) ? blk : -1;
 }
 
-template <typename T, int STAGES>
-__global__ void __launch_bounds__(kThreads) paged_decode_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_item;
-  __shared__ int s_last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int num_items = p.ctrl[kCtrlNumItems];
-  const int64_t chunk = p.ctrl[kCtrlChunk];
-  const uint32_t wbase = smem_u32(smem + warp * STAGES * kStageBytes);
-  const int64_t row_stride = (int64_t)p.num_kv_heads * kRowBytes;  // bytes between slots
+// The visible KV extent of request r: [lo, hi) and its tile origin.
+struct Extent {
+  int64_t qs, lo, hi, base;
+};
+__device__ __forceinline__ Extent extent_of(const DecodeParams& p, int64_t r) {
+  Extent e;
+  e.qs = __ldg(p.qsl + r);
+  e.lo = max(__ldg(p.qstart + e.qs), (int64_t)0);
+  e.hi = __ldg(p.ctx_len + r);
+  e.base = e.lo & ~(int64_t)15;
+  return e;
+}
 
-  for (;;) {
-    if (threadIdx.x == 0) s_item = atomicAdd(p.cursor, 1);
-    __syncthreads();
-    const int item = s_item;
-    if (item >= num_items) break;
+// CTA holding global tile x when N tiles are split over G CTAs.
+__device__ __forceinline__ int64_t cta_of(int64_t x, int64_t n_all, int64_t grid) {
+  return ((x + 1) * grid - 1) / n_all;
+}
 
-    // ---- locate the item ----
-    const int h = item % p.num_kv_heads;
-    const int64_t unit = item / p.num_kv_heads;
-    int64_t lo_i = 0, hi_i = p.num_requests;  // largest r with unit_prefix[r] <= unit
-    while (lo_i < hi_i) {
-      const int64_t mid = (lo_i + hi_i) >> 1;
-      if (__ldg(p.unit_prefix + mid) <= unit)
-        lo_i = mid + 1;
-      else
-        hi_i = mid;
+struct Slot {  // per-stage header written by the producer
+  int32_t vr;         // virtual request: group * R + r
+  int32_t tile;       // tile index inside the request
+  uint32_t row_mask;  // bit i: row i holds a visible, valid key
+  int32_t pad;
+};
+
+// ------------------------------------------------------------ producer
+__device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
+                        uint8_t* ring, Slot* slots, uint32_t full0, uint32_t empty0,
+                        int32_t stage_bytes, int32_t plane_stride, int32_t rowp) {
+  const int lane = threadIdx.x & 31;
+  const int hb = p.heads_per_cta;
+  const int row = lane & 15, plane = lane >> 4;
+  const uint32_t copy_bytes = hb * kHeadRow;
+  int64_t r = __ldg(p.cta_start + blockIdx.x);
+  int64_t group = first / tiles;
+  Extent e = extent_of(p, r);
+  int64_t req_lo = __ldg(p.tile_prefix + r), req_hi = __ldg(p.tile_prefix + r + 1);
+  const int64_t* trow = p.table + r * p.table_stride;
+  int k = 0;
+  for (int64_t x = first; x < last; ++x, ++k) {
+    const int64_t g = x / tiles, local = x - g * tiles;
+    if (g != group || local >= req_hi) {  // next request (skip those with no tiles)
+      if (g != group) {
+        group = g;
+        r = 0;
+      }
+      req_lo = __ldg(p.tile_prefix + r);
+      req_hi = __ldg(p.tile_prefix + r + 1);
+      while (local >= req_hi) {
+        ++r;
+        req_lo = req_hi;
+        req_hi = __ldg(p.tile_prefix + r + 1);
+      }
+      e = extent_of(p, r);
+      trow = p.table + r * p.table_stride;
     }
-    const int64_t r = lo_i - 1;
-    const int64_t u0 = __ldg(p.unit_prefix + r);
-    const int split = (int)(unit - u0);
-    const int nsplit = (int)(__ldg(p.unit_prefix + r + 1) - u0);
-    const int64_t qs = __ldg(p.qsl + r);
-    const int ncols = (int)(__ldg(p.qsl + r + 1) - qs) * p.group;
-    const int64_t lo_r = max(__ldg(p.qstart + qs), (int64_t)0);
-    const int64_t hi_r = __ldg(p.ctx_len + r);
-    const bool empty_history = hi_r <= lo_r;
-    const int64_t tile0 = (lo_r & ~(int64_t)15) + (int64_t)split * chunk;
-    const int64_t kv_begin = max(tile0, lo_r);
-    const int64_t kv_end = min(tile0 + chunk, hi_r);
-    const int ntiles = kv_end > kv_begin ? (int)((kv_end - tile0 + 15) >> 4) : 0;
-    const int64_t* trow = p.table + r * p.table_stride;
-
-    // Visible window of this lane's two columns (2c, 2c+1).
-    int64_t wlo[2], whi[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int n = 2 * c + j;
-      if (n < ncols) {
-        const int64_t t = qs + n / p.group;
-        wlo[j] = max(lo_r, __ldg(p.qstart + t));
-        whi[j] = min(hi_r - 1, __ldg(p.qpos + t));
-      } else {
-        wlo[j] = 1;
-        whi[j] = 0;
-      }
+    const int s = k % kStages;
+    if (!mbar_wait(empty0 + 8 * s, ((k / kStages) & 1) ^ 1, p.status)) {
+      // A consumer stopped: let the copies already issued land before the
+      // CTA leaves (each wait is bounded again).
+      for (int i = k - kStages > 0 ? k - kStages : 0; i < k; ++i)
+        mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, nullptr);
+      return;
     }
-    // Q^T as B fragments: column g = (query g / group, head g % group).
-    uint32_t qb[8][2];
-    if (g < ncols) {
-      const int64_t t = qs + g / p.group;
-      const int hq = h * p.group + g % p.group;
-      const char* qrow = p.query + t * p.q_st_bytes + (int64_t)hq * p.q_sh_bytes;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        qb[ks][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * ks + 2 * c) * 2));
-        qb[ks][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * ks + 2 * c + 8) * 2));
-      }
-    } else {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) qb[ks][0] = qb[ks][1] = 0u;
+    const int64_t tile = local - req_lo;
+    const int64_t pos = e.base + tile * kTile + row;
+    int64_t off = 0;
+    const int64_t blk = (pos >= e.lo && pos < e.hi) ? page_of(p, trow, pos, &off) : -2;
+    const bool valid = blk >= 0;
+    if (blk == -1 && p.status != nullptr) atomicOr(p.status, MVB_STATUS_BLOCK_OUT_OF_RANGE);
+    const uint32_t mask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
+    if (lane == 0) {
+      slots[s] = Slot{(int32_t)(group * p.num_requests + r), (int32_t)tile, mask, 0};
+      mbar_expect_tx(full0 + 8 * s, 2 * kTile * copy_bytes);
     }
-
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    float o[8][4];
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-
-    const int nt = ntiles > warp ? (ntiles - 1 - warp) / kWarps + 1 : 0;
-    const bool one_page_per_tile = p.bs_shift >= 4;
-
-    // Issue the cp.async copies of local tile i into ring slot i % STAGES.
-    auto issue = [&](int i) {
-      const int64_t tstart = tile0 + (int64_t)(warp + kWarps * i) * kTileTokens;
-      const uint32_t kdst = wbase + (i % STAGES) * kStageBytes;
-      const int ch = lane & 15;
-      int64_t off0 = 0, blk0 = -1;
-      if (one_page_per_tile) blk0 = page_of(p, trow, tstart, &off0);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int row = 2 * jj + (lane >> 4);
-        const int64_t pos = tstart + row;
-        int64_t blk, off;
-        if (one_page_per_tile) {
-          blk = blk0;
-          off = off0 + row;
-        } else {
-          blk = page_of(p, trow, pos, &off);
-        }
-        const bool valid = blk >= 0 && pos >= kv_begin && pos < kv_end;
-        const char* src =
-            valid ? p.cache + (blk * p.block_size + off) * row_stride + (int64_t)h * kRowBytes + ch * 16
-                  : p.cache;
-        const uint32_t dst = kdst + row * kRowBytes + ((ch ^ (row & 7)) << 4);
-        cp_async_16(dst, src, valid);
-        cp_async_16(dst + kTileBytes, src + p.plane_bytes * valid, valid);
-      }
-    };
-
-#pragma unroll
-    for (int i = 0; i < STAGES - 1; ++i) {
-      if (i < nt) issue(i);
-      cp_async_commit();
-    }
-    for (int i = 0; i < nt; ++i) {
-      cp_async_wait<STAGES - 2>();
-      __syncwarp();
-      if (i + STAGES - 1 < nt) issue(i + STAGES - 1);
-      cp_async_commit();
-
-      const uint32_t kb = wbase + (i % STAGES) * kStageBytes;
-      const uint32_t vb = kb + kTileBytes;
-      const int64_t tstart = tile0 + (int64_t)(warp + kWarps * i) * kTileTokens;
-
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int ch = 2 * ks + (lane >> 4);
-        uint32_t a[4];
-        ldsm_x4(kb + row * kRowBytes + ((ch ^ (row & 7)) << 4), a);
-        mma16816<T>(s, a, qb[ks][0], qb[ks][1]);
-      }
-
-      // Mask: token rows g and g+8 of the tile, columns 2c and 2c+1.
-      const int64_t p0 = tstart + g, p1 = p0 + 8;
-      const bool in0 = p0 >= kv_begin && p0 < kv_end, in1 = p1 >= kv_begin && p1 < kv_end;
-      bool ok0, ok1;
-      {
-        int64_t off;
-        if (one_page_per_tile) {
-          const bool page_ok = page_of(p, trow, tstart, &off) >= 0;
-          ok0 = in0 && page_ok;
-          ok1 = in1 && page_ok;
-        } else {
-          ok0 = in0 && page_of(p, trow, p0, &off) >= 0;
-          ok1 = in1 && page_of(p, trow, p1, &off) >= 0;
-        }
-        if (p.status != nullptr && (ok0 != in0 || ok1 != in1))
-          atomicOr(p.status, MVB_STATUS_BLOCK_OUT_OF_RANGE);
-      }
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        s[j] = (ok0 && p0 >= wlo[j] && p0 <= whi[j]) ? s[j] * p.scale_log2 : -INFINITY;
-        s[2 + j] = (ok1 && p1 >= wlo[j] && p1 <= whi[j]) ? s[2 + j] * p.scale_log2 : -INFINITY;
-      }
-      float corr[2], pr[4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float tmax = fmaxf(s[j], s[2 + j]);
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-        const float mn = fmaxf(m[j], tmax);
-        const float mu = mn == -INFINITY ? 0.f : mn;
-        corr[j] = exp2f(m[j] - mu);
-        pr[j] = exp2f(s[j] - mu);
-        pr[2 + j] = exp2f(s[2 + j] - mu);
-        l[j] = l[j] * corr[j] + pr[j] + pr[2 + j];
-        m[j] = mn;
-      }
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        o[mt][0] *= corr[0];
-        o[mt][1] *= corr[1];
-        o[mt][2] *= corr[0];
-        o[mt][3] *= corr[1];
-      }
-      const uint32_t pb0 = movmatrix_t(pack2<T>(pr[0], pr[1]));
-      const uint32_t pb1 = movmatrix_t(pack2<T>(pr[2], pr[3]));
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int row = (lane & 7) + (lane >> 4) * 8;
-        const int ch = 2 * mt + ((lane >> 3) & 1);
-        uint32_t a[4];
-        ldsm_x4_t(vb + row * kRowBytes + ((ch ^ (row & 7)) << 4), a);
-        mma16816<T>(o[mt], a, pb0, pb1);
-      }
-    }
-    cp_async_wait<0>();
-
-    // ---- merge the four warps ----
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      l[j] += __shfl_xor_sync(0xffffffffu, l[j], 4);
-      l[j] += __shfl_xor_sync(0xffffffffu, l[j], 8);
-      l[j] += __shfl_xor_sync(0xffffffffu, l[j], 16);
-    }
-    __syncthreads();  // every warp is done with its ring: reuse it
-    float* so = reinterpret_cast<float*>(smem);             // [warp][col][kColStride]
-    float2* sml = reinterpret_cast<float2*>(so + kWarps * kDecodeCols * kColStride);  // [warp][col]
-    {
-      float* mine = so + warp * kDecodeCols * kColStride;
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        mine[(2 * c) * kColStride + 16 * mt + g] = o[mt][0];
-        mine[(2 * c + 1) * kColStride + 16 * mt + g] = o[mt][1];
-        mine[(2 * c) * kColStride + 16 * mt + g + 8] = o[mt][2];
-        mine[(2 * c + 1) * kColStride + 16 * mt + g + 8] = o[mt][3];
-      }
-      if (g == 0) {
-        sml[warp * kDecodeCols + 2 * c] = make_float2(m[0], l[0]);
-        sml[warp * kDecodeCols + 2 * c + 1] = make_float2(m[1], l[1]);
-      }
-    }
-    __syncthreads();
-
-    const int d = threadIdx.x;  // one head-dim element per thread
-    for (int n = 0; n < ncols; ++n) {
-      float mx = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, sml[w * kDecodeCols + n].x);
-      const float mu = mx == -INFINITY ? 0.f : mx;
-      float acc = 0.f, sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float2 ml = sml[w * kDecodeCols + n];
-        const float f = exp2f(ml.x - mu);
-        acc += so[(w * kDecodeCols + n) * kColStride + d] * f;
-        sum += ml.y * f;
-      }
-      if (nsplit == 1) {
-        const int64_t t = qs + n / p.group;
-        const int hq = h * p.group + n % p.group;
-        const float v = empty_history ? 0.f : (sum > 0.f ? acc / sum : NAN);
-        reinterpret_cast<T*>(p.out)[(t * p.num_q_heads + hq) * kDecodeHeadDim + d] =
-            from_float<T>(v);
-      } else {
-        p.partial_o[((int64_t)item * kDecodeCols + n) * kDecodeHeadDim + d] = acc;
-        if (d == 0) p.partial_ml[(int64_t)item * kDecodeCols + n] = make_float2(mx, sum);
-      }
-    }
-
-    if (nsplit > 1) {
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const int done = atomicAdd(p.merge_count + r * p.num_kv_heads + h, 1);
-        s_last = done == nsplit - 1;
-      }
-      __syncthreads();
-      if (s_last) {
-        __threadfence();
-        for (int n = 0; n < ncols; ++n) {
-          float mx = -INFINITY;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const int64_t it = (u0 + sp) * p.num_kv_heads + h;
-            mx = fmaxf(mx, __ldcg(&p.partial_ml[it * kDecodeCols + n].x));
-          }
-          const float mu = mx == -INFINITY ? 0.f : mx;
-          float acc = 0.f, sum = 0.f;
-          for (int sp = 0; sp < nsplit; ++sp) {
-            const int64_t it = (u0 + sp) * p.num_kv_heads + h;
-            const float2 ml = __ldcg(&p.partial_ml[it * kDecodeCols + n]);
-            const float f = exp2f(ml.x - mu);
-            acc += __ldcg(&p.partial_o[(it * kDecodeCols + n) * kDecodeHeadDim + d]) * f;
-            sum += ml.y * f;
-          }
-          const int64_t t = qs + n / p.group;
-          const int hq = h * p.group + n % p.group;
-          reinterpret_cast<T*>(p.out)[(t * p.num_q_heads + hq) * kDecodeHeadDim + d] =
-              from_float<T>(sum > 0.f ? acc / sum : NAN);
-        }
-      }
-    }
-    __syncthreads();  // merge buffer and s_item are reused by the next item
+    __syncwarp();
+    const char* src =
+        valid ? p.cache + plane * p.plane_bytes +
+                    ((blk * p.block_size + off) * p.num_kv_heads + group * hb) * kHeadRow
+              : p.zero_row;
+    bulk_g2s(smem_u32(ring + s * stage_bytes + plane * plane_stride + row * rowp), src, copy_bytes,
+             full0 + 8 * s);
   }
 }
 
-template <typename T, int STAGES>
-int launch_typed(const DecodeParams& dp, cudaStream_t stream) {
-  const int smem = STAGES * kWarps * kStageBytes;
-  static_assert(kWarps * kDecodeCols * (kColStride + 2) * 4 <= STAGES * kWarps * kStageBytes,
-                "merge buffer must fit in the ring");
-  static int configured_device = -1;
-  static int grid = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<T, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return MVB_ERR_CUDA;
+// ------------------------------------------------------------ consumer
+template <typename T>
+__device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
+                        int64_t n_all, const uint8_t* ring, const Slot* slots, uint32_t full0,
+                        uint32_t empty0, int32_t stage_bytes, int32_t plane_stride, int32_t rowp) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int hb = p.heads_per_cta;
+  const int64_t grid = gridDim.x;
+
+  int64_t cur_vr = -1, r = 0, seg_first = 0, req_tiles = 0;
+  int kvh = 0, ncols = 0;
+  Extent e{0, 0, 0, 0};
+  int64_t wlo[2] = {1, 1}, whi[2] = {0, 0};
+  uint32_t qb[8][2];
+  float m[2], l[2], o[8][4];
+
+  int k = 0;
+  for (int64_t x = first; x < last; ++x, ++k) {
+    const int s = k % kStages;
+    if (!mbar_wait(full0 + 8 * s, (k / kStages) & 1, p.status)) return;
+    const Slot slot = slots[s];
+    if (slot.vr != cur_vr) {  // a new request segment starts in this CTA
+      cur_vr = slot.vr;
+      const int64_t grp = cur_vr / p.num_requests;
+      r = cur_vr - grp * p.num_requests;
+      kvh = (int)grp * hb + w;
+      e = extent_of(p, r);
+      ncols = (int)(__ldg(p.qsl + r + 1) - e.qs) * p.group;
+      req_tiles = __ldg(p.tile_prefix + r + 1) - __ldg(p.tile_prefix + r);
+      seg_first = slot.tile;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int n = 2 * c + j;
+        if (n < ncols) {
+          const int64_t t = e.qs + n / p.group;
+          wlo[j] = max(e.lo, __ldg(p.qstart + t));
+          whi[j] = min(e.hi - 1, __ldg(p.qpos + t));
+        } else {
+          wlo[j] = 1;
+          whi[j] = 0;
+        }
+      }
+      if (g < ncols) {
+        const int64_t t = e.qs + g / p.group;
+        const int hq = kvh * p.group + g % p.group;
+        const char* qrow = p.query + t * p.q_st_bytes + (int64_t)hq * p.q_sh_bytes;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          qb[ks][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * ks + 2 * c) * 2));
+          qb[ks][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + (16 * ks + 2 * c + 8) * 2));
+        }
+      } else {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) qb[ks][0] = qb[ks][1] = 0u;
+      }
+      m[0] = m[1] = -INFINITY;
+      l[0] = l[1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     }
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<T, STAGES>,
-                                                      kThreads, smem);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return MVB_ERR_CUDA;
+
+    // ---- one 16-token tile of KV head kvh ----
+    const uint32_t kb = smem_u32(ring + s * stage_bytes) + w * kHeadRow;
+    const uint32_t vb = kb + plane_stride;
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+      uint32_t a[4];
+      ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, a);
+      mma16816<T>(sc, a, qb[ks][0], qb[ks][1]);
     }
-    grid = num_sms() * (per_sm > 0 ? per_sm : 1);
-    configured_device = dev;
+    const int64_t p0 = e.base + (int64_t)slot.tile * kTile + g, p1 = p0 + 8;
+    const bool ok0 = (slot.row_mask >> g) & 1u, ok1 = (slot.row_mask >> (g + 8)) & 1u;
+    float corr[2], pr[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float s0 = (ok0 && p0 >= wlo[j] && p0 <= whi[j]) ? sc[j] * p.scale_log2 : -INFINITY;
+      const float s1 =
+          (ok1 && p1 >= wlo[j] && p1 <= whi[j]) ? sc[2 + j] * p.scale_log2 : -INFINITY;
+      float tmax = fmaxf(s0, s1);
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+      const float mn = fmaxf(m[j], tmax);
+      const float mu = mn == -INFINITY ? 0.f : mn;
+      corr[j] = exp2f(m[j] - mu);
+      pr[j] = exp2f(s0 - mu);
+      pr[2 + j] = exp2f(s1 - mu);
+      l[j] = l[j] * corr[j] + pr[j] + pr[2 + j];
+      m[j] = mn;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o[mt][0] *= corr[0];
+      o[mt][1] *= corr[1];
+      o[mt][2] *= corr[0];
+      o[mt][3] *= corr[1];
+    }
+    const uint32_t pb0 = movmatrix_t(pack2<T>(pr[0], pr[1]));
+    const uint32_t pb1 = movmatrix_t(pack2<T>(pr[2], pr[3]));
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int row = (lane & 7) + (lane >> 4) * 8;
+      uint32_t a[4];
+      ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, a);
+      mma16816<T>(o[mt], a, pb0, pb1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+
+    // ---- end of this CTA's segment of the request ----
+    const bool req_done = slot.tile == req_tiles - 1;
+    if (!req_done && x != last - 1) continue;
+    float lsum[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float v = l[j];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      lsum[j] = v;
+    }
+    const bool empty_history = e.hi <= e.lo;
+    if (seg_first == 0 && req_done) {  // whole request in this CTA: write O / l
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int n = 2 * c + j;
+        if (n >= ncols) continue;
+        const float inv = lsum[j] > 0.f ? 1.f / lsum[j] : NAN;
+        const int64_t t = e.qs + n / p.group;
+        const int hq = kvh * p.group + n % p.group;
+        T* orow = reinterpret_cast<T*>(p.out) + (t * p.num_q_heads + hq) * kDecodeHeadDim;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          orow[16 * mt + g] = from_float<T>(empty_history ? 0.f : o[mt][j] * inv);
+          orow[16 * mt + g + 8] = from_float<T>(empty_history ? 0.f : o[mt][2 + j] * inv);
+        }
+      }
+      continue;
+    }
+    // Partial: slot 0 when this request is the first one of the CTA's share.
+    const int pslot = (seg_first == slot.tile - (x - first)) ? 0 : 1;
+    const int64_t pidx = ((int64_t)blockIdx.x * 2 + pslot) * kMaxHeadsPerCta + w;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = 2 * c + j;
+      float* po = p.partial_o + (pidx * kDecodeCols + n) * kDecodeHeadDim;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        po[16 * mt + g] = o[mt][j];
+        po[16 * mt + g + 8] = o[mt][2 + j];
+      }
+      if (g == 0) p.partial_ml[pidx * kDecodeCols + n] = make_float2(m[j], lsum[j]);
+    }
+    __threadfence();
+    __syncwarp();
+    int done = 0;
+    if (lane == 0) done = atomicAdd(p.merge_count + r * p.num_kv_heads + kvh, 1);
+    done = __shfl_sync(0xffffffffu, done, 0);
+    const int64_t grp = cur_vr / p.num_requests;
+    const int64_t g0 = grp * tiles + __ldg(p.tile_prefix + r);
+    const int64_t g1 = g0 + req_tiles;
+    const int64_t b_first = cta_of(g0, n_all, grid), b_last = cta_of(g1 - 1, n_all, grid);
+    // Segments = CTAs in [b_first, b_last] with a non-empty share (shares
+    // are empty only when there are fewer tiles than CTAs).
+    int nseg = 0;
+    for (int64_t b = b_first; b <= b_last; ++b)
+      nseg += (b * n_all / grid) < ((b + 1) * n_all / grid);
+    if (done != nseg - 1) continue;
+    // Last segment to finish: merge all segments of (request, kvh).
+    __threadfence();
+    for (int n = 0; n < ncols; ++n) {
+      float mx = -INFINITY;
+      for (int64_t b = b_first; b <= b_last; ++b) {
+        const int64_t bstart = b * n_all / grid;
+        if (bstart == (b + 1) * n_all / grid) continue;  // empty share
+        const int64_t bfirst_vr = (bstart / tiles) * p.num_requests + __ldg(p.cta_start + b);
+        const int sl = (bfirst_vr == cur_vr) ? 0 : 1;
+        const int64_t idx = (b * 2 + sl) * kMaxHeadsPerCta + w;
+        mx = fmaxf(mx, __ldcg(&p.partial_ml[idx * kDecodeCols + n].x));
+      }
+      const float mu = mx == -INFINITY ? 0.f : mx;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float sum = 0.f;
+      for (int64_t b = b_first; b <= b_last; ++b) {
+        const int64_t bstart = b * n_all / grid;
+        if (bstart == (b + 1) * n_all / grid) continue;  // empty share
+        const int64_t bfirst_vr = (bstart / tiles) * p.num_requests + __ldg(p.cta_start + b);
+        const int sl = (bfirst_vr == cur_vr) ? 0 : 1;
+        const int64_t idx = (b * 2 + sl) * kMaxHeadsPerCta + w;
+        const float2 ml = __ldcg(&p.partial_ml[idx * kDecodeCols + n]);
+        const float f = exp2f(ml.x - mu);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                                    p.partial_o + (idx * kDecodeCols + n) * kDecodeHeadDim) +
+                                lane);
+        acc.x += v.x * f;
+        acc.y += v.y * f;
+        acc.z += v.z * f;
+        acc.w += v.w * f;
+        sum += ml.y * f;
+      }
+      const float inv = sum > 0.f ? 1.f / sum : NAN;
+      const int64_t t = e.qs + n / p.group;
+      const int hq = kvh * p.group + n % p.group;
+      T* orow = reinterpret_cast<T*>(p.out) + (t * p.num_q_heads + hq) * kDecodeHeadDim + 4 * lane;
+      orow[0] = from_float<T>(empty_history ? 0.f : acc.x * inv);
+      orow[1] = from_float<T>(empty_history ? 0.f : acc.y * inv);
+      orow[2] = from_float<T>(empty_history ? 0.f : acc.z * inv);
+      orow[3] = from_float<T>(empty_history ? 0.f : acc.w * inv);
+    }
   }
-  paged_decode_kernel<T, STAGES><<<grid, kThreads, smem, stream>>>(dp);
-  return check_launch();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
+    paged_decode_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(8) uint64_t bars[2 * kStages];
+  __shared__ Slot slots[kStages];
+  const int hb = p.heads_per_cta;
+  const int32_t rowp = hb * kHeadRow + 16;
+  const int32_t plane_stride = kTile * rowp;
+  const int32_t stage_bytes = 2 * plane_stride;
+  const int64_t tiles = p.ctrl[kCtrlTiles];
+  const int64_t n_all = tiles * (p.num_kv_heads / hb);
+  const int64_t grid = gridDim.x;
+  const int64_t first = (int64_t)blockIdx.x * n_all / grid;
+  const int64_t last = ((int64_t)blockIdx.x + 1) * n_all / grid;
+  const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kStages]);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, hb);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+  if (first >= last) return;
+  const int warp = threadIdx.x >> 5;
+  if (warp == hb) {
+    produce(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride, rowp);
+  } else {
+    consume<T>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
+               plane_stride, rowp);
+  }
+}
+
+int set_up(const void* fn, int smem, int threads, int* per_sm) {
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, fn, threads, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return MVB_ERR_CUDA;
+  }
+  return MVB_OK;
 }
 
 }  // namespace
 
-int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w) {
+int heads_per_cta(int32_t num_kv_heads) {
+  for (int hb = kMaxHeadsPerCta; hb > 1; --hb)
+    if (num_kv_heads % hb == 0) return hb;
+  return 1;
+}
+
+int decode_grid(const AttentionProblem& a, int* smem_bytes) {
+  const int hb = heads_per_cta(a.num_kv_heads);
+  const int smem = kStages * 2 * kTile * (hb * kHeadRow + 16);
+  const int threads = 32 * (hb + 1);
+  static int cached_device = -1, cached_hb = -1, cached_grid = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_device || hb != cached_hb) {
+    int per_sm_h = 0, per_sm_b = 0;
+    if (set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half>), smem, threads,
+               &per_sm_h) != MVB_OK ||
+        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16>), smem, threads,
+               &per_sm_b) != MVB_OK)
+      return -1;
+    int per_sm = per_sm_h < per_sm_b ? per_sm_h : per_sm_b;
+    if (per_sm < 1) per_sm = 1;
+    int grid = num_sms() * per_sm;
+    cached_grid = grid < kMaxDecodeCtas ? grid : kMaxDecodeCtas;
+    cached_device = dev;
+    cached_hb = hb;
+  }
+  *smem_bytes = smem;
+  return cached_grid;
+}
+
+int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w, int32_t grid,
+                        int32_t smem_bytes) {
   char* ws = static_cast<char*>(a.workspace);
   DecodeParams dp;
-  const int eb = 2;
   dp.query = static_cast<const char*>(a.query);
-  dp.q_st_bytes = a.q_st * eb;
-  dp.q_sh_bytes = a.q_sh * eb;
+  dp.q_st_bytes = a.q_st * 2;
+  dp.q_sh_bytes = a.q_sh * 2;
   dp.out = static_cast<char*>(a.out);
   dp.cache = static_cast<const char*>(a.cache);
-  dp.plane_bytes = a.num_blocks * a.block_size * (int64_t)a.num_kv_heads * kRowBytes;
+  dp.plane_bytes = a.num_blocks * a.block_size * (int64_t)a.num_kv_heads * kHeadRow;
   dp.num_blocks = a.num_blocks;
   dp.block_size = a.block_size;
   dp.bs_shift = (a.block_size & (a.block_size - 1)) == 0 ? __builtin_ctz(a.block_size) : -1;
   dp.num_kv_heads = a.num_kv_heads;
+  dp.heads_per_cta = heads_per_cta(a.num_kv_heads);
   dp.group = a.num_q_heads / a.num_kv_heads;
   dp.num_q_heads = a.num_q_heads;
   dp.qpos = a.qpos;
@@ -491,16 +580,22 @@ int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w) {
   dp.table_width = a.table_width;
   dp.num_requests = a.num_requests;
   dp.scale_log2 = a.scale * 1.4426950408889634f;
-  dp.ctrl = reinterpret_cast<const int32_t*>(ws + w.ctrl);
-  dp.cursor = reinterpret_cast<int32_t*>(ws + w.ctrl) + kCtrlCursor;
-  dp.unit_prefix = reinterpret_cast<const int32_t*>(ws + w.unit_prefix);
+  dp.ctrl = reinterpret_cast<const int64_t*>(ws + w.ctrl);
+  dp.tile_prefix = reinterpret_cast<const int64_t*>(ws + w.tile_prefix);
+  dp.cta_start = reinterpret_cast<const int32_t*>(ws + w.cta_start);
   dp.merge_count = reinterpret_cast<int32_t*>(ws + w.merge_count);
+  dp.zero_row = ws + w.zero_row;
   dp.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
   dp.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
   dp.status = a.status;
-  if (a.dtype == MVB_DTYPE_F16) return launch_typed<__half, 3>(dp, a.stream);
-  if (a.dtype == MVB_DTYPE_BF16) return launch_typed<__nv_bfloat16, 3>(dp, a.stream);
-  return MVB_ERR_UNSUPPORTED_DTYPE;
+  const int threads = 32 * (dp.heads_per_cta + 1);
+  if (a.dtype == MVB_DTYPE_F16)
+    paged_decode_kernel<__half><<<grid, threads, smem_bytes, a.stream>>>(dp);
+  else if (a.dtype == MVB_DTYPE_BF16)
+    paged_decode_kernel<__nv_bfloat16><<<grid, threads, smem_bytes, a.stream>>>(dp);
+  else
+    return MVB_ERR_UNSUPPORTED_DTYPE;
+  return check_launch();
 }
 
 }  // namespace mvb

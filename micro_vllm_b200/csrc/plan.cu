@@ -2,13 +2,15 @@
 // kernel's work decomposition without a host round trip, so a step can be
 // captured in a CUDA graph and replayed with new metadata.
 //
-// Block 0 classifies every request, picks the split size and writes, per
-// request, the prefix sum of its decode units (KV splits).  Decode item i
-// is unit i / num_kv_heads of KV head i % num_kv_heads, so consecutive items
-// are the KV heads of the same pages: CTAs that run together read adjacent
-// 256-byte head rows of one 2 KiB token row.  The remaining blocks zero the
-// output rows of tokens that belong to no request (graph padding), which the
-// Triton backend gets from torch.zeros_like (triton_paged.py:343).
+// Block 0 classifies every request and lays the KV of all decode-class
+// requests out as one sequence of 16-token tiles (per request: the
+// positions from its visibility start rounded down to 16, to its context
+// length).  It writes the per-request tile prefix sums and, for each decode
+// CTA b, the request holding the first tile of b's equal share
+// [b*N/G, (b+1)*N/G) of the N tiles — the stream-K split the decode kernel
+// walks.  The other blocks zero the output rows of tokens owned by no
+// request (graph padding), which the Triton backend gets from
+// torch.zeros_like (triton_paged.py:343).
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
 
@@ -16,8 +18,6 @@ namespace mvb {
 namespace {
 
 constexpr int kPlanThreads = 1024;
-// Longest context a request may have (2^30 tokens); keeps split sizes in int32.
-constexpr int64_t kMaxContext = (int64_t)1 << 30;
 
 struct PlanParams {
   const int64_t* qsl;
@@ -25,44 +25,44 @@ struct PlanParams {
   const int64_t* ctx_len;
   int64_t num_requests;
   int64_t num_tokens;
-  int32_t num_kv_heads;
   int32_t group;
   int32_t num_q_heads;
   int32_t head_dim;
   int32_t elem_bytes;
+  int32_t num_kv_heads;
+  int32_t heads_per_cta;
+  int32_t decode_ctas;
   void* out;
-  int32_t* ctrl;
-  int32_t* unit_prefix;
+  int64_t* ctrl;
+  int64_t* tile_prefix;
+  int32_t* cta_start;
   int32_t* kind;
   int32_t* merge_count;
-  int64_t unit_cap;
-  PlanTuning tuning;
+  uint4* zero_row;
 };
 
-// Aligned KV extent of decode-class request r: [base, hi) with base = lo
-// rounded down to 16 so that 16-token tiles line up with 16-token pages.
-__device__ __forceinline__ void request_extent(const PlanParams& p, int64_t r, int32_t* kind,
-                                               int64_t* span) {
+// Class and decode tile count of request r.
+__device__ __forceinline__ int64_t request_tiles(const PlanParams& p, int64_t r, int32_t* kind) {
   const int64_t qs = p.qsl[r], qe = p.qsl[r + 1];
   const int64_t len = qe - qs;
-  *span = 0;
   // Zero-length (graph padding) or malformed ranges own no work.
   if (len <= 0 || qs < 0 || qe > p.num_tokens) {
     *kind = kKindNone;
-    return;
+    return 0;
   }
   if (len * p.group > kDecodeCols) {
     *kind = kKindPrefill;
-    return;
+    return 0;
   }
-  *kind = kKindDecode;
   const int64_t lo = max(p.qstart[qs], (int64_t)0);
   const int64_t hi = p.ctx_len[r];
   if (hi > kMaxContext) {  // beyond any pool: refuse rather than overflow
     *kind = kKindNone;
-    return;
+    return 0;
   }
-  *span = hi > lo ? hi - (lo & ~(int64_t)15) : 0;
+  *kind = kKindDecode;
+  const int64_t span = hi > lo ? hi - (lo & ~(int64_t)15) : 0;
+  return span > 0 ? (span + 15) >> 4 : 1;  // an empty history still owns one (empty) tile
 }
 
 // Block-wide inclusive scan of one int64 per thread (1024 threads).
@@ -95,7 +95,8 @@ __device__ __forceinline__ int64_t block_inclusive_scan(int64_t v, int64_t* warp
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
   if (blockIdx.x > 0) {
     // Zero rows of tokens outside [qsl[0], qsl[R]).
-    const int64_t covered_lo = p.num_requests > 0 ? min(max(p.qsl[0], (int64_t)0), p.num_tokens) : 0;
+    const int64_t covered_lo =
+        p.num_requests > 0 ? min(max(p.qsl[0], (int64_t)0), p.num_tokens) : 0;
     const int64_t covered_hi =
         p.num_requests > 0 ? min(max(p.qsl[p.num_requests], covered_lo), p.num_tokens) : 0;
     const int64_t row_words = (int64_t)p.num_q_heads * p.head_dim * p.elem_bytes / 4;
@@ -111,67 +112,57 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
 
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t total;
-  __shared__ int64_t red[2];
 
-  // Pass 1: total aligned decode span and number of decode requests.
-  int64_t span_sum = 0, dec_count = 0;
-  for (int64_t r = threadIdx.x; r < p.num_requests; r += kPlanThreads) {
-    int32_t k;
-    int64_t span;
-    request_extent(p, r, &k, &span);
-    p.kind[r] = k;
-    span_sum += span;
-    dec_count += (k == kKindDecode);
-  }
-  if (threadIdx.x < 2) red[threadIdx.x] = 0;
-  __syncthreads();
-  atomicAdd(reinterpret_cast<unsigned long long*>(&red[0]), (unsigned long long)span_sum);
-  atomicAdd(reinterpret_cast<unsigned long long*>(&red[1]), (unsigned long long)dec_count);
-  __syncthreads();
-  span_sum = red[0];
-  dec_count = red[1];
-
-  // Split size: about target_items items over all KV heads, clamped, then
-  // raised until sum(ceil(span/chunk)) <= span_sum/chunk + dec_count fits.
-  int64_t chunk = (span_sum * p.num_kv_heads + p.tuning.target_items - 1) / p.tuning.target_items;
-  chunk = max(chunk, (int64_t)p.tuning.min_chunk);
-  chunk = min(chunk, (int64_t)p.tuning.max_chunk);
-  const int64_t room = p.unit_cap - dec_count;  // >= 1, checked by the host
-  chunk = max(chunk, (span_sum + room - 1) / max(room, (int64_t)1));
-  chunk = max((chunk + 15) & ~(int64_t)15, (int64_t)16);
-
-  // Pass 2: per-request unit counts and their exclusive prefix sum.
+  // Per-request tile counts and their exclusive prefix sum.
   int64_t running = 0;
   for (int64_t base = 0; base < p.num_requests; base += kPlanThreads) {
     const int64_t r = base + threadIdx.x;
-    int64_t units = 0;
+    int64_t tiles = 0;
     if (r < p.num_requests) {
       int32_t k;
-      int64_t span;
-      request_extent(p, r, &k, &span);
-      if (k == kKindDecode) units = span > 0 ? (span + chunk - 1) / chunk : 1;
+      tiles = request_tiles(p, r, &k);
+      p.kind[r] = k;
     }
-    const int64_t incl = block_inclusive_scan(units, warp_tot, &total);
-    if (r < p.num_requests) p.unit_prefix[r] = (int32_t)(running + incl - units);
+    const int64_t incl = block_inclusive_scan(tiles, warp_tot, &total);
+    if (r < p.num_requests) p.tile_prefix[r] = running + incl - tiles;
     running += total;
     __syncthreads();
   }
+  if (threadIdx.x == 0) {
+    p.tile_prefix[p.num_requests] = running;
+    p.ctrl[kCtrlTiles] = running;
+  }
   for (int64_t i = threadIdx.x; i < p.num_requests * p.num_kv_heads; i += kPlanThreads)
     p.merge_count[i] = 0;
-  if (threadIdx.x == 0) {
-    p.unit_prefix[p.num_requests] = (int32_t)running;
-    p.ctrl[kCtrlNumUnits] = (int32_t)running;
-    p.ctrl[kCtrlNumItems] = (int32_t)(running * p.num_kv_heads);
-    p.ctrl[kCtrlCursor] = 0;
-    p.ctrl[kCtrlPrefillCursor] = 0;
-    p.ctrl[kCtrlChunk] = (int32_t)chunk;
+  if (threadIdx.x < kMaxHeadsPerCta * 256 / 16) p.zero_row[threadIdx.x] = make_uint4(0, 0, 0, 0);
+  __syncthreads();  // tile_prefix complete before the searches below
+
+  // Request holding the first tile of each decode CTA's share.
+  const int64_t groups = p.num_kv_heads / p.heads_per_cta;
+  const int64_t n_all = running * groups;
+  for (int b = threadIdx.x; b < p.decode_ctas; b += kPlanThreads) {
+    const int64_t first = (int64_t)b * n_all / p.decode_ctas;
+    int32_t r_first = 0;
+    if (running > 0 && first < n_all) {
+      const int64_t local = first % running;
+      int64_t lo = 0, hi = p.num_requests;  // largest r with tile_prefix[r] <= local
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (p.tile_prefix[mid] <= local)
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      r_first = (int32_t)(lo - 1);
+    }
+    p.cta_start[b] = r_first;
   }
 }
 
 }  // namespace
 
 int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t group,
-                const PlanTuning& tuning) {
+                int32_t decode_ctas) {
   char* ws = static_cast<char*>(a.workspace);
   PlanParams p;
   p.qsl = a.qsl;
@@ -179,18 +170,20 @@ int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t gro
   p.ctx_len = a.ctx_len;
   p.num_requests = a.num_requests;
   p.num_tokens = a.num_tokens;
-  p.num_kv_heads = a.num_kv_heads;
   p.group = group;
   p.num_q_heads = a.num_q_heads;
   p.head_dim = a.head_dim;
   p.elem_bytes = elem_bytes_of(a.dtype);
+  p.num_kv_heads = a.num_kv_heads;
+  p.heads_per_cta = heads_per_cta(a.num_kv_heads);
+  p.decode_ctas = decode_ctas;
   p.out = a.out;
-  p.ctrl = reinterpret_cast<int32_t*>(ws + w.ctrl);
-  p.unit_prefix = reinterpret_cast<int32_t*>(ws + w.unit_prefix);
+  p.ctrl = reinterpret_cast<int64_t*>(ws + w.ctrl);
+  p.tile_prefix = reinterpret_cast<int64_t*>(ws + w.tile_prefix);
+  p.cta_start = reinterpret_cast<int32_t*>(ws + w.cta_start);
   p.kind = reinterpret_cast<int32_t*>(ws + w.kind);
   p.merge_count = reinterpret_cast<int32_t*>(ws + w.merge_count);
-  p.unit_cap = w.unit_cap;
-  p.tuning = tuning;
+  p.zero_row = reinterpret_cast<uint4*>(ws + w.zero_row);
   // Block 0 plans; 32 more blocks zero padding rows (enough for a few MB).
   plan_kernel<<<33, kPlanThreads, 0, a.stream>>>(p);
   return check_launch();
