@@ -138,6 +138,40 @@ MVB_API int mvb_attention_forward(const void* query, int64_t query_token_stride,
                           int32_t num_q_heads, float scale, int32_t dtype, void* workspace,
                           size_t workspace_bytes, int32_t* status, void* stream);
 
+/*
+ * mvb_paged_attention for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference project: it exists for hosts that cannot
+ * hand the library a workspace — a plugin host whose device memory belongs
+ * to its own arena allocator and that forbids other allocations, a serving
+ * loop that must not risk an allocation failing or blocking mid-run, or a
+ * language binding with no access to CUDA memory management.
+ *
+ * Same arguments and results as mvb_paged_attention minus the workspace.
+ * The scratch it needs lives in a 24 MiB region compiled into the library,
+ * which every GPU that loads the library holds until the process exits.
+ * Batches needing more (mvb_paged_attention_workspace_size above 24 MiB,
+ * i.e. tens of thousands of requests) are rejected with
+ * MVB_ERR_WORKSPACE_TOO_SMALL.  The first call on each device looks up the
+ * region's device address (cudaGetSymbolAddress with that device current);
+ * make that first call before any stream capture.  All calls share the
+ * region: calls whose GPU work overlaps (different streams or host threads
+ * on one device) race and must be serialised by the caller.
+ */
+MVB_API int mvb_paged_attention_no_alloc(const void* query, int64_t query_token_stride,
+                                         int64_t query_head_stride, void* output,
+                                         const void* kv_cache, int64_t num_blocks,
+                                         int32_t block_size, int32_t num_kv_heads,
+                                         int32_t head_dim, const int64_t* query_positions,
+                                         const int64_t* query_context_starts,
+                                         const int64_t* query_start_locations,
+                                         const int64_t* context_lengths,
+                                         const int64_t* block_table,
+                                         int64_t block_table_row_stride,
+                                         int64_t block_table_width, int64_t num_tokens,
+                                         int64_t num_requests, int32_t num_q_heads, float scale,
+                                         int32_t dtype, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _P, _SZ, _P, _P,  # workspace, bytes, status, stream
         ],
     ),
+    "mvb_paged_attention_no_alloc": (
+        ctypes.c_int,
+        [
+            _P, _I64, _I64,  # query, token stride, head stride
+            _P,  # output
+            _P, _I64, _I32, _I32, _I32,  # cache, num_blocks, block_size, Hkv, D
+            _P, _P, _P, _P, _P, _I64, _I64,  # metadata, table stride/width
+            _I64, _I64, _I32, _F32, _I32,  # T, R, Hq, scale, dtype
+            _P, _P,  # status, stream
+        ],
+    ),
     "mvb_attention_forward": (
         ctypes.c_int,
         [
