@@ -11,7 +11,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 
-WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads) {
+WorkspaceLayout workspace_layout(int64_t num_requests, int64_t num_tokens, int32_t num_kv_heads) {
   WorkspaceLayout w;
   size_t off = 0;
   w.ctrl = off;
@@ -31,16 +31,19 @@ WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads) {
   off += align256(partials * sizeof(float2));
   w.partial_o = off;
   off += align256(partials * kDecodeHeadDim * sizeof(float));
+  w.prefill_prefix = off;
+  off += align256((size_t)(num_requests + 1) * sizeof(int64_t));
+  w.prefill_unit_req = off;  // at most one prefill unit per token plus one per request
+  off += align256((size_t)(num_tokens + num_requests) * sizeof(int32_t));
   w.end = off;
   return w;
 }
 
 size_t workspace_bytes_for(int64_t max_tokens, int64_t max_requests, int32_t num_q_heads,
                            int32_t num_kv_heads, int32_t head_dim) {
-  (void)max_tokens;
   (void)num_q_heads;
   (void)head_dim;
-  return workspace_layout(max_requests, num_kv_heads).end;
+  return workspace_layout(max_requests, max_tokens, num_kv_heads).end;
 }
 
 int num_sms() {
@@ -68,17 +71,19 @@ int run_paged_attention(const AttentionProblem& p) {
 
   if (p.workspace == nullptr || ((uintptr_t)p.workspace % 256) != 0)
     return MVB_ERR_INVALID_ARGUMENT;
-  const WorkspaceLayout w = workspace_layout(p.num_requests, p.num_kv_heads);
+  const WorkspaceLayout w = workspace_layout(p.num_requests, p.num_tokens, p.num_kv_heads);
   if (p.workspace_bytes < w.end) return MVB_ERR_WORKSPACE_TOO_SMALL;
   int smem = 0;
   const int grid = decode_grid(p, &smem);
   if (grid <= 0) return MVB_ERR_CUDA;
 
-  int rc = launch_plan(p, w, group, grid);
+  const bool tc_prefill = prefill_tc_supported(p);
+  int rc = launch_plan(p, w, group, grid, tc_prefill ? 128 / group : 0);
   if (rc != MVB_OK) return rc;
   rc = launch_paged_decode(p, w, grid, smem);
   if (rc != MVB_OK) return rc;
   // Requests whose query chunk does not fit the decode tile.
+  if (tc_prefill) return launch_paged_prefill(p, w);
   const int32_t* kind = reinterpret_cast<const int32_t*>(static_cast<char*>(p.workspace) + w.kind);
   return launch_paged_attention_generic(p, kind, kKindPrefill);
 }

@@ -52,16 +52,19 @@ constexpr int32_t kStatusWaitTimeout = 4;
 
 // ctrl[] words (int64).
 enum CtrlWord : int {
-  kCtrlTiles = 0,   // decode tiles per KV-head group
+  kCtrlTiles = 0,          // decode tiles per KV-head group
+  kCtrlPrefillUnits = 1,   // prefill query tiles (items = units x num_kv_heads)
+  kCtrlPrefillCursor = 2,  // prefill work cursor (low 32 bits used)
   kCtrlWords = 32,
 };
 
-// Workspace carve-up.  Offsets depend only on (num_requests, num_kv_heads).
+// Workspace carve-up.  Offsets depend on (num_requests, num_tokens, num_kv_heads).
 struct WorkspaceLayout {
-  size_t ctrl, tile_prefix, cta_start, kind, merge_count, zero_row, partial_ml, partial_o, end;
+  size_t ctrl, tile_prefix, cta_start, kind, merge_count, zero_row, partial_ml, partial_o;
+  size_t prefill_prefix, prefill_unit_req, end;
 };
 
-WorkspaceLayout workspace_layout(int64_t num_requests, int32_t num_kv_heads);
+WorkspaceLayout workspace_layout(int64_t num_requests, int64_t num_tokens, int32_t num_kv_heads);
 size_t workspace_bytes_for(int64_t max_tokens, int64_t max_requests, int32_t num_q_heads,
                            int32_t num_kv_heads, int32_t head_dim);
 
@@ -83,8 +86,14 @@ int heads_per_cta(int32_t num_kv_heads);
 // Decode grid for this device and problem (also what the planner assumes).
 int decode_grid(const AttentionProblem& p, int* smem_bytes);
 
+// True when the tensor-core prefill kernel can take this problem (head_dim
+// 128, fp16/bf16, group dividing 128, pages of a multiple of 16 tokens,
+// TMA-compatible alignment); its query tile is 128/group tokens.
+bool prefill_tc_supported(const AttentionProblem& p);
+int launch_paged_prefill(const AttentionProblem& p, const WorkspaceLayout& w);
+
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,
-                int32_t decode_ctas);
+                int32_t decode_ctas, int32_t prefill_block_q);
 int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w, int32_t grid,
                         int32_t smem_bytes);
 

@@ -46,10 +46,10 @@ extern "C" MVB_API int mvb_paged_attention_no_alloc(
     const int64_t* block_table, int64_t block_table_row_stride, int64_t block_table_width,
     int64_t num_tokens, int64_t num_requests, int32_t num_q_heads, float scale, int32_t dtype,
     int32_t* status, void* stream) {
-  if (num_requests < 0 || num_kv_heads <= 0) return MVB_ERR_INVALID_ARGUMENT;
+  if (num_requests < 0 || num_tokens < 0 || num_kv_heads <= 0) return MVB_ERR_INVALID_ARGUMENT;
   // The batch must fit the built-in region (the same layout a caller-provided
   // workspace would get).
-  if (mvb::workspace_layout(num_requests, num_kv_heads).end > kNoAllocScratchBytes)
+  if (mvb::workspace_layout(num_requests, num_tokens, num_kv_heads).end > kNoAllocScratchBytes)
     return MVB_ERR_WORKSPACE_TOO_SMALL;
 
   int device = 0;

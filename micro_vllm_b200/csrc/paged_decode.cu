@@ -35,6 +35,8 @@
 // HBM bandwidth).
 #include <math.h>
 
+#include <type_traits>
+
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
 
@@ -361,14 +363,26 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
       o[mt][2] *= corr[0];
       o[mt][3] *= corr[1];
     }
-    const uint32_t pb0 = movmatrix_t(pack2<T>(pr[0], pr[1]));
-    const uint32_t pb1 = movmatrix_t(pack2<T>(pr[2], pr[3]));
+    const uint32_t ph0 = pack2<T>(pr[0], pr[1]), ph1 = pack2<T>(pr[2], pr[3]);
+    const uint32_t pb0 = movmatrix_t(ph0);
+    const uint32_t pb1 = movmatrix_t(ph1);
+    // bf16 keeps 8 mantissa bits: P = P_hi + P_lo (both bf16) and a second
+    // P.V product restore ~16 bits, matching the fp16 path's accuracy.
+    constexpr bool kSplitP = std::is_same<T, __nv_bfloat16>::value;
+    uint32_t pl0 = 0, pl1 = 0;
+    if constexpr (kSplitP) {
+      const float2 h0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ph0));
+      const float2 h1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ph1));
+      pl0 = movmatrix_t(pack2<T>(pr[0] - h0.x, pr[1] - h0.y));
+      pl1 = movmatrix_t(pack2<T>(pr[2] - h1.x, pr[3] - h1.y));
+    }
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const int row = (lane & 7) + (lane >> 4) * 8;
       uint32_t a[4];
       ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, a);
       mma16816<T>(o[mt], a, pb0, pb1);
+      if constexpr (kSplitP) mma16816<T>(o[mt], a, pl0, pl1);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);

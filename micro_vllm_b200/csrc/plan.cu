@@ -32,6 +32,7 @@ struct PlanParams {
   int32_t num_kv_heads;
   int32_t heads_per_cta;
   int32_t decode_ctas;
+  int32_t prefill_block_q;  // 0: prefill-class requests go to the CUDA-core kernel
   void* out;
   int64_t* ctrl;
   int64_t* tile_prefix;
@@ -39,6 +40,8 @@ struct PlanParams {
   int32_t* kind;
   int32_t* merge_count;
   uint4* zero_row;
+  int64_t* prefill_prefix;
+  int32_t* prefill_unit_req;
 };
 
 // Class and decode tile count of request r.
@@ -50,16 +53,16 @@ __device__ __forceinline__ int64_t request_tiles(const PlanParams& p, int64_t r,
     *kind = kKindNone;
     return 0;
   }
-  if (len * p.group > kDecodeCols) {
-    *kind = kKindPrefill;
-    return 0;
-  }
-  const int64_t lo = max(p.qstart[qs], (int64_t)0);
   const int64_t hi = p.ctx_len[r];
   if (hi > kMaxContext) {  // beyond any pool: refuse rather than overflow
     *kind = kKindNone;
     return 0;
   }
+  if (len * p.group > kDecodeCols) {
+    *kind = kKindPrefill;
+    return 0;
+  }
+  const int64_t lo = max(p.qstart[qs], (int64_t)0);
   *kind = kKindDecode;
   const int64_t span = hi > lo ? hi - (lo & ~(int64_t)15) : 0;
   return span > 0 ? (span + 15) >> 4 : 1;  // an empty history still owns one (empty) tile
@@ -113,24 +116,38 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t total;
 
-  // Per-request tile counts and their exclusive prefix sum.
-  int64_t running = 0;
+  // Per-request decode tile counts and prefill query-tile counts, and their
+  // exclusive prefix sums.
+  int64_t running = 0, running_units = 0;
   for (int64_t base = 0; base < p.num_requests; base += kPlanThreads) {
     const int64_t r = base + threadIdx.x;
-    int64_t tiles = 0;
+    int64_t tiles = 0, units = 0;
     if (r < p.num_requests) {
       int32_t k;
       tiles = request_tiles(p, r, &k);
       p.kind[r] = k;
+      if (k == kKindPrefill && p.prefill_block_q > 0)
+        units = (p.qsl[r + 1] - p.qsl[r] + p.prefill_block_q - 1) / p.prefill_block_q;
     }
     const int64_t incl = block_inclusive_scan(tiles, warp_tot, &total);
     if (r < p.num_requests) p.tile_prefix[r] = running + incl - tiles;
     running += total;
     __syncthreads();
+    const int64_t incl_u = block_inclusive_scan(units, warp_tot, &total);
+    const int64_t first_unit = running_units + incl_u - units;
+    if (r < p.num_requests) {
+      p.prefill_prefix[r] = first_unit;
+      for (int64_t u = 0; u < units; ++u) p.prefill_unit_req[first_unit + u] = (int32_t)r;
+    }
+    running_units += total;
+    __syncthreads();
   }
   if (threadIdx.x == 0) {
     p.tile_prefix[p.num_requests] = running;
+    p.prefill_prefix[p.num_requests] = running_units;
     p.ctrl[kCtrlTiles] = running;
+    p.ctrl[kCtrlPrefillUnits] = running_units;
+    p.ctrl[kCtrlPrefillCursor] = 0;
   }
   for (int64_t i = threadIdx.x; i < p.num_requests * p.num_kv_heads; i += kPlanThreads)
     p.merge_count[i] = 0;
@@ -162,7 +179,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
 }  // namespace
 
 int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t group,
-                int32_t decode_ctas) {
+                int32_t decode_ctas, int32_t prefill_block_q) {
   char* ws = static_cast<char*>(a.workspace);
   PlanParams p;
   p.qsl = a.qsl;
@@ -177,6 +194,7 @@ int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t gro
   p.num_kv_heads = a.num_kv_heads;
   p.heads_per_cta = heads_per_cta(a.num_kv_heads);
   p.decode_ctas = decode_ctas;
+  p.prefill_block_q = prefill_block_q;
   p.out = a.out;
   p.ctrl = reinterpret_cast<int64_t*>(ws + w.ctrl);
   p.tile_prefix = reinterpret_cast<int64_t*>(ws + w.tile_prefix);
@@ -184,6 +202,8 @@ int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t gro
   p.kind = reinterpret_cast<int32_t*>(ws + w.kind);
   p.merge_count = reinterpret_cast<int32_t*>(ws + w.merge_count);
   p.zero_row = reinterpret_cast<uint4*>(ws + w.zero_row);
+  p.prefill_prefix = reinterpret_cast<int64_t*>(ws + w.prefill_prefix);
+  p.prefill_unit_req = reinterpret_cast<int32_t*>(ws + w.prefill_unit_req);
   // Block 0 plans; 32 more blocks zero padding rows (enough for a few MB).
   plan_kernel<<<33, kPlanThreads, 0, a.stream>>>(p);
   return check_launch();

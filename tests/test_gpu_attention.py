@@ -287,3 +287,73 @@ def test_physical_placement_does_not_change_the_output() -> None:
     rows = [0, 17, 99, 255]
     snap_batch = paged_batch(num_blocks=40000, seed=1, **kw)
     _run_and_check(snap_batch, rows=rows, op=op)
+
+
+def _nan_fill_page_tails(batch) -> None:
+    """Poison the unused slots after each request's context in its last page
+    (and nothing the operator reads as a visible key)."""
+
+    bs = batch.metadata.block_size
+    table = batch.metadata.block_table.cpu()
+    for r, c in enumerate(batch.context_lengths):
+        if c % bs:
+            page = int(table[r, (c - 1) // bs])
+            batch.cache[:, page, c % bs:] = float("nan")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("num_q_heads,num_kv_heads", [(16, 8), (32, 8), (8, 8), (64, 8), (16, 2)])
+def test_prefill_tensor_core_path_matches_oracle(dtype, num_q_heads, num_kv_heads) -> None:
+    """Chunked prefill on the tcgen05 kernel: fresh prompts, chunks over a
+    cached prefix (prefix-cache hits), chunk lengths that are not a multiple
+    of the query tile, NaN-poisoned page tails."""
+
+    ctx = [700, 1500, 300, 129, 2100, 64]
+    qlen = [700, 333, 300, 65, 1024, 64]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=num_q_heads,
+        num_kv_heads=num_kv_heads, head_dim=128, block_size=16, num_blocks=2000,
+        dtype=dtype, device=DEV, seed=num_q_heads + num_kv_heads,
+    )
+    _nan_fill_page_tails(batch)
+    out = _run_and_check(batch)
+    assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("block_size", [32, 48, 256])
+def test_prefill_tensor_core_path_other_page_sizes(block_size: int) -> None:
+    ctx = [900, 257, 1200]
+    qlen = [900, 100, 17]
+    nb = sum(-(-c // block_size) for c in ctx) + 8
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=block_size, num_blocks=nb, dtype=torch.float16, device=DEV, seed=block_size,
+    )
+    _run_and_check(batch)
+
+
+@pytest.mark.parametrize("window", [1, 50, 300])
+def test_prefill_sliding_window_on_tensor_cores(window: int) -> None:
+    ctx = [1000, 640]
+    qlen = [1000, 200]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=200, dtype=torch.bfloat16, device=DEV, seed=window, window=window,
+    )
+    _nan_fill_page_tails(batch)
+    _run_and_check(batch)
+
+
+def test_prefill_repeated_calls_reuse_the_workspace() -> None:
+    """Several different mixed batches through one operator instance (the
+    persistent kernels' barrier phases and work cursors restart cleanly)."""
+
+    op = B200PagedAttentionOperator()
+    for seed in range(4):
+        ctx = uniform_lengths(6, 1, 1500, seed=seed) + [800]
+        qlen = [min(c, q) for c, q in zip(ctx, uniform_lengths(6, 1, 300, seed=seed + 9))] + [800]
+        batch = paged_batch(
+            context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+            block_size=16, num_blocks=1000, dtype=torch.float16, device=DEV, seed=100 + seed,
+        )
+        _run_and_check(batch, op=op)
