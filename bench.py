@@ -55,6 +55,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--workload", choices=("decode", "mixed"), default="decode",
+                    help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
     return ap.parse_args()
@@ -247,18 +249,25 @@ def run_ours(args) -> None:
     dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     elsize = 2
 
-    ctx = context_lengths(args.ctx, BATCH_PER_GPU, seed=1000 + rank)
+    # The global batch (256 sequences per GPU) is split over the ranks by
+    # whole sequences, longest-first to the least-loaded rank.
+    from micro_vllm_b200.partition import partition_sequences, sequence_work
+
+    global_ctx = context_lengths(args.ctx, BATCH_PER_GPU * world, seed=1000)
+    shards = partition_sequences([sequence_work(c) for c in global_ctx], world)
+    ctx = [global_ctx[i] for i in shards[rank].indices]
+    local_batch = len(ctx)
     if args.pool_gb is None:
         nb = pool_blocks_for_fraction(POOL_FRACTION, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, dtype, dev)
     else:
         nb = int(args.pool_gb * 1e9) // (2 * BLOCK_SIZE * NUM_KV_HEADS * HEAD_DIM * elsize)
     batch = paged_batch(
-        context_lengths=ctx, query_lengths=[1] * BATCH_PER_GPU, num_q_heads=NUM_Q_HEADS,
+        context_lengths=ctx, query_lengths=[1] * local_batch, num_q_heads=NUM_Q_HEADS,
         num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE, num_blocks=nb,
         dtype=dtype, device=dev, seed=2000 + rank,
     )
     op = B200PagedAttentionOperator()
-    op.reserve(dev, max_num_tokens=BATCH_PER_GPU, max_num_requests=BATCH_PER_GPU,
+    op.reserve(dev, max_num_tokens=local_batch, max_num_requests=local_batch,
                num_q_heads=NUM_Q_HEADS, num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM)
     stream = torch.cuda.current_stream(dev)
 
@@ -278,7 +287,7 @@ def run_ours(args) -> None:
 
     # Attention-only entry point (plan + decode), to time the decode kernel.
     md = batch.metadata
-    ws, st = op._workspace(dev, BATCH_PER_GPU, BATCH_PER_GPU, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM)
+    ws, st = op._workspace(dev, local_batch, local_batch, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM)
     out_buf = torch.empty_like(batch.query)
     lib = _lib.load()
     attn_args = (
@@ -287,7 +296,7 @@ def run_ours(args) -> None:
         md.query_positions.data_ptr(), md.query_context_start_positions.data_ptr(),
         md.query_start_locations.data_ptr(), md.context_lengths.data_ptr(),
         md.block_table.data_ptr(), md.block_table.stride(0), md.block_table.shape[1],
-        BATCH_PER_GPU, BATCH_PER_GPU, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
+        local_batch, local_batch, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
         _lib.MVB_DTYPE_F16 if dtype == torch.float16 else _lib.MVB_DTYPE_BF16,
         ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream,
     )
@@ -358,8 +367,8 @@ def run_ours(args) -> None:
         barrier()
         e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.steps)
 
-    attn_bytes = decode_bytes(ctx, elsize)
-    step_bytes_all = attn_bytes * world  # every rank runs the same-size workload
+    attn_bytes = decode_bytes(ctx, elsize)  # this rank's share
+    step_bytes_all = decode_bytes(global_ctx, elsize)  # the whole job
     value = step_bytes_all / (step_ms * 1e-3) / 1e9
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peak, peak_src = 6650.0, "fallback"
@@ -386,7 +395,7 @@ def run_ours(args) -> None:
                 f"pool {POOL_FRACTION:.0%} of HBM ({nb} blocks), random block tables; step = KV scatter + decode"
             ),
             "global_batch": BATCH_PER_GPU * world,
-            "parallelism": f"sequence-partitioned replicas x{world}",
+            "parallelism": f"whole-sequence LPT partition over {world} GPU replicas, no data-path collective",
             "l2": "inputs larger than L2 (KV per step about %.2f GB vs 126 MB L2); no flush" % (attn_bytes / 1e9),
             "bytes_per_step_per_gpu": attn_bytes,
         },
@@ -408,9 +417,11 @@ def run_ours(args) -> None:
             "d2h_bytes_per_step": d2h,
             "ms_per_step": e2e_ms,
         },
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 4 * args.steps * world,
         "clocks": clock_info,
     }
+    if world > 1:
+        line["config"]["shard_imbalance"] = max(s.work for s in shards) / (sum(s.work for s in shards) / world)
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, elsize, args.cpu_sample_seconds)
     if world > 1:
@@ -420,10 +431,124 @@ def run_ours(args) -> None:
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- config 3
+def prefill_flops(prefix: list[int], new: list[int], num_q_heads: int, head_dim: int) -> int:
+    """Algorithmic flops of causal attention for chunks of `new` tokens over
+    `prefix` cached tokens: 4*D per visible (query, key) pair per head."""
+
+    pairs = sum(l * p + l * (l + 1) // 2 for p, l in zip(prefix, new))
+    return 4 * head_dim * num_q_heads * pairs
+
+
+def run_mixed(args) -> None:
+    """8 prefill chunks of 2048 new tokens over cached
+    prefixes U[0,1024] + 120 decodes at ctx U[256,2048], 16/8/128, bf16.
+    Reports the prefill kernel's tensor throughput (prefill requests alone,
+    attention-only entry point) and the whole mixed step's time."""
+
+    import torch
+
+    from micro_vllm_b200 import B200PagedAttentionOperator
+    from micro_vllm_b200 import _lib
+    from micro_vllm_b200.workloads import paged_batch, uniform_lengths
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dtype = torch.bfloat16  # config 3 is specified in bf16
+    prefix = uniform_lengths(8, 0, 1024, seed=31)
+    new = [2048] * 8
+    dec_ctx = uniform_lengths(120, 256, 2048, seed=32)
+    ctx = [p + n for p, n in zip(prefix, new)] + dec_ctx
+    qlen = new + [1] * 120
+    need = sum(-(-c // BLOCK_SIZE) for c in ctx)
+    nb = max(need + 64, int((args.pool_gb or 4.0) * 1e9) // (2 * BLOCK_SIZE * NUM_KV_HEADS * HEAD_DIM * 2))
+    mixed = paged_batch(context_lengths=ctx, query_lengths=qlen, num_q_heads=NUM_Q_HEADS,
+                        num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE,
+                        num_blocks=nb, dtype=dtype, device=dev, seed=33)
+    prefill_only = paged_batch(context_lengths=ctx[:8], query_lengths=qlen[:8], num_q_heads=NUM_Q_HEADS,
+                               num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE,
+                               num_blocks=nb, dtype=dtype, device=dev, seed=34)
+    op = B200PagedAttentionOperator()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+
+    def attention_only(batch, out):
+        md = batch.metadata
+        ws, st = op._workspace(dev, batch.query.shape[0], batch.num_requests, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM)
+        rc = lib.mvb_paged_attention(
+            batch.query.data_ptr(), batch.query.stride(0), batch.query.stride(1), out.data_ptr(),
+            batch.cache.data_ptr(), batch.cache.shape[1], BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM,
+            md.query_positions.data_ptr(), md.query_context_start_positions.data_ptr(),
+            md.query_start_locations.data_ptr(), md.context_lengths.data_ptr(),
+            md.block_table.data_ptr(), md.block_table.stride(0), md.block_table.shape[1],
+            batch.query.shape[0], batch.num_requests, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
+            _lib.MVB_DTYPE_BF16, ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream)
+        _lib.check(rc, "bench attention")
+
+    def timed(fn, steps):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / steps
+
+    out_p = torch.empty_like(prefill_only.query)
+    # Write the prefill chunks' K/V once so the attention-only timing sees the real cache.
+    op(prefill_only.query, prefill_only.key, prefill_only.value, prefill_only.cache, prefill_only.metadata)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    prefill_ms = timed(lambda: attention_only(prefill_only, out_p), args.steps)
+    mixed_ms = timed(lambda: op(mixed.query, mixed.key, mixed.value, mixed.cache, mixed.metadata), args.steps)
+    clock_info = clocks.stop()
+    flops = prefill_flops(prefix, new, NUM_Q_HEADS, HEAD_DIM)
+    achieved = flops / (prefill_ms * 1e-3) / 1e12
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peak, peak_src = 1590.0, "fallback"
+    if peaks_path.exists():
+        peak, peak_src = float(json.loads(peaks_path.read_text())["bf16_tflops"]), "measured"
+    dec_bytes = decode_bytes(dec_ctx, 2)
+    line = {
+        "metric": "prefill_attn_TFLOPs",
+        "value": achieved,
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": prefill_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": "BASELINE config 3: 8 prefill chunks x 2048 new tokens over cached prefixes "
+                        "U[0,1024] + 120 decodes ctx U[256,2048], 16/8/128, bs 16, causal",
+            "prefix_tokens": prefix,
+            "prefill_flops": flops,
+            "l2": "prefill re-reads K/V per query tile from L2/HBM; no flush",
+        },
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "kernel": "paged_prefill_kernel (with planner; prefill requests only)"},
+        "mixed_step": {"ms": mixed_ms, "decode_bytes": dec_bytes,
+                       "note": "scatter of 16504 tokens + plan + decode (120 seqs) + prefill (8 chunks)"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mixed":
+        run_mixed(args)
     else:
         run_ours(args)
 

@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a PTX the prefill kernel uses: mbarriers,
-// TMA tile loads (no multicast), tcgen05 MMA / TMEM access and the shared
+// per-CTA TMA tile loads, tcgen05 MMA / TMEM access and the shared
 // memory matrix descriptors of the 5th-generation tensor cores.
 #pragma once
 
