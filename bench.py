@@ -57,6 +57,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload", choices=("decode", "mixed"), default="decode",
                     help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
+    ap.add_argument("--mixed-fp16", action="store_true",
+                    help="with --workload mixed and --dtype fp16: run config 3 in fp16")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
     return ap.parse_args()
@@ -454,7 +456,9 @@ def run_mixed(args) -> None:
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    dtype = torch.bfloat16  # config 3 is specified in bf16
+    # Config 3 is specified in bf16 (the default here); --dtype fp16 runs the
+    # same batch in fp16 (the prefill target is quoted against fp16 peak).
+    dtype = torch.float16 if args.dtype == "fp16" and args.mixed_fp16 else torch.bfloat16
     prefix = uniform_lengths(8, 0, 1024, seed=31)
     new = [2048] * 8
     dec_ctx = uniform_lengths(120, 256, 2048, seed=32)
@@ -482,7 +486,8 @@ def run_mixed(args) -> None:
             md.query_start_locations.data_ptr(), md.context_lengths.data_ptr(),
             md.block_table.data_ptr(), md.block_table.stride(0), md.block_table.shape[1],
             batch.query.shape[0], batch.num_requests, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
-            _lib.MVB_DTYPE_BF16, ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream)
+            _lib.MVB_DTYPE_BF16 if dtype == torch.bfloat16 else _lib.MVB_DTYPE_F16,
+            ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream)
         _lib.check(rc, "bench attention")
 
     def timed(fn, steps):
@@ -523,7 +528,7 @@ def run_mixed(args) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16" if dtype == torch.bfloat16 else "f16",
         "data": "synthetic",
         "config": {
             "workload": "BASELINE config 3: 8 prefill chunks x 2048 new tokens over cached prefixes "

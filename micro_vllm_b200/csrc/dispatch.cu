@@ -78,7 +78,7 @@ int run_paged_attention(const AttentionProblem& p) {
   if (grid <= 0) return MVB_ERR_CUDA;
 
   const bool tc_prefill = prefill_tc_supported(p);
-  int rc = launch_plan(p, w, group, grid, tc_prefill ? 128 / group : 0);
+  int rc = launch_plan(p, w, group, grid, tc_prefill ? prefill_tokens_per_unit(group) : 0);
   if (rc != MVB_OK) return rc;
   rc = launch_paged_decode(p, w, grid, smem);
   if (rc != MVB_OK) return rc;

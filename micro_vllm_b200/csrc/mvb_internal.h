@@ -88,8 +88,10 @@ int decode_grid(const AttentionProblem& p, int* smem_bytes);
 
 // True when the tensor-core prefill kernel can take this problem (head_dim
 // 128, fp16/bf16, group dividing 128, pages of a multiple of 16 tokens,
-// TMA-compatible alignment); its query tile is 128/group tokens.
+// TMA-compatible alignment).
 bool prefill_tc_supported(const AttentionProblem& p);
+// Query tokens per prefill work unit (a pair of 128-row query tiles).
+int prefill_tokens_per_unit(int32_t group);
 int launch_paged_prefill(const AttentionProblem& p, const WorkspaceLayout& w);
 
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,

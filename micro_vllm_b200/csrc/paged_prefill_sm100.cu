@@ -1,14 +1,15 @@
 // Varlen causal chunked-prefill attention over the paged cache on the
 // 5th-generation tensor cores (tcgen05 + TMEM), head_dim 128, fp16/bf16.
 //
-// Work item = (prefill-class request, 128-row query tile, KV head): the 128
-// MMA rows are 128/G query tokens x the G query heads of one GQA group, so
-// every K/V tile fetched serves the whole group.  A persistent grid (one
-// CTA per SM, 224 KB of shared memory, 512 TMEM columns) pulls items from an
-// atomic cursor, heaviest (latest) query tiles first.
+// Work item = (prefill-class request, pair of 128-row query tiles, KV head).
+// Each tile's 128 MMA rows are 128/G query tokens x the G query heads of one
+// GQA group; the two tiles (A: the earlier tokens, B: the next ones) share
+// every K/V tile fetched.  A persistent grid (one CTA per SM, 193 KB of
+// shared memory, all 512 TMEM columns) pulls items from an atomic cursor,
+// heaviest (latest) query tiles first.
 //
-// Roles inside a CTA (6 warps):
-//   warp 0  TMA producer: the Q tile once per item (a 3-D tensor map over
+// Roles inside a CTA (10 warps):
+//   warp 0  TMA producer: both Q tiles once per item (a 3-D tensor map over
 //           [token, head, dim] so the G heads of a token land in adjacent
 //           rows) and, per 128-key KV tile, the 8 pages of K and V (a 2-D
 //           tensor map over the cache's [2*NB*bs slots, Hkv*128] view; one
@@ -16,25 +17,33 @@
 //           2-stage ring, 128-byte swizzled — the layout the tensor cores
 //           read directly.  Pages missing from the block table are fetched
 //           from page 0 and masked.
-//   warp 1  MMA issuer (one thread): S_j = Q.K_j^T into one of two TMEM
-//           score buffers, then O += P_{j-1}.V_{j-1} with O resident in TMEM
-//           (kind::f16, M=128, N=128, K=16 steps; V is read MN-major).
-//   warps 2-5  softmax: one thread per row (= TMEM lane).  Each loads its
-//           128 scores with tcgen05.ld, applies the causal / visibility
-//           window mask, keeps an fp32 online softmax whose reference max
-//           moves only when a new max exceeds it by 2^8 (then O is rescaled
-//           in TMEM with tcgen05.ld/st — rare after the first tiles), writes
-//           P in the swizzled K-major layout the PV MMA reads, zeroes V rows
-//           no query may see (so stale cache bytes cannot reach O through
-//           0 * NaN), and at the end normalises O and stores it.
+//   warp 1  MMA issuer (one thread), ping-pong between the tiles:
+//             S_A(0), S_B(0); then per KV tile j:
+//             PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
+//           S_X = Q_X.K^T lands in TMEM (128 fp32 columns per tile); the
+//           softmax writes P_X back over S_X as packed 16-bit pairs and
+//           PV_X: O_X += P_X.V_j reads it straight from TMEM (A operand in
+//           TMEM, V from shared memory MN-major).  tcgen05 operations of one
+//           thread complete in issue order, so S_X(j+1) finishing implies
+//           PV_X(j) finished.
+//   warps 2-5 / 6-9  softmax of tile A / B, one thread per row (= TMEM
+//           lane): pass 1 loads the 128 scores and takes the masked max;
+//           the reference max moves only when the tile max exceeds it by
+//           2^8, and then O_X is rescaled in TMEM (no wait needed: O_X holds
+//           PV_X(j-1), complete since S_X(j) is); pass 2 reloads the scores,
+//           computes P = 2^(s - max) and stores it to TMEM.  bf16 P is split
+//           into P_hi + P_lo (two MMAs) to keep ~16 bits.  Tile A's warps
+//           also zero V rows no query of the pair may see, so stale cache
+//           bytes cannot reach O as 0 * NaN.  At the end each row's O is
+//           normalised and stored.
 // Every mbarrier wait is bounded; a timeout sets kStatusWaitTimeout and the
 // kernel winds down.
 //
 // Semantics are those of ReferenceAttentionOperator.forward
 // (reference.py:14-81), as in the decode kernel: token t of request r sees
 // max(ctx_start[first token of r], ctx_start[t]) .. min(ctx_len[r]-1, pos[t]).
-// Roofline: tensor cores; algorithmic flops per item = 4 * D * (visible
-// query-key pairs) * heads.
+// Roofline: tensor cores; algorithmic flops per request = 4 * D * Hq *
+// (visible query-key pairs).
 #include <math.h>
 
 #include <type_traits>
@@ -48,32 +57,32 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kRows = 128;                     // MMA M
-constexpr int kKeys = 128;                     // keys per KV tile
-constexpr int kHalf = kRows * 128;             // one [128 rows][64 elem] swizzled half: 16 KiB
-constexpr int kTileBytes = 2 * kHalf;          // [128][128] fp16/bf16: 32 KiB
-constexpr int kStageBytes = 2 * kTileBytes;    // K + V
+constexpr int kRows = 128;                   // MMA M: rows of one query tile
+constexpr int kKeys = 128;                   // keys per KV tile
+constexpr int kHalf = kRows * 128;           // [128 rows][64 elem] swizzled half: 16 KiB
+constexpr int kTileBytes = 2 * kHalf;        // [128][128] 16-bit: 32 KiB
+constexpr int kStageBytes = 2 * kTileBytes;  // K + V
 constexpr int kStages = 2;
-constexpr int kOffQ = 0;
-constexpr int kOffKv = kTileBytes;
-constexpr int kOffP = kOffKv + kStages * kStageBytes;
-constexpr int kSmemUsed = kOffP + 2 * kTileBytes;  // Q + 2 KV stages + P (hi, lo) = 224 KiB
-constexpr int kSmemBytes = kSmemUsed + 1024;       // + alignment slack
-constexpr int kThreads = 192;
+constexpr int kOffQ = 0;                     // Q_A, Q_B
+constexpr int kOffKv = 2 * kTileBytes;
+constexpr int kSmemUsed = kOffKv + kStages * kStageBytes;  // 192 KiB
+constexpr int kSmemBytes = kSmemUsed + 1024;               // + alignment slack
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 256;  // S buffers at columns 0 and 128, O at 256
+// TMEM columns: S/P of tile A and B, then O of tile A and B.
+__device__ __forceinline__ uint32_t col_s(int t) { return 128u * (uint32_t)t; }
+__device__ __forceinline__ uint32_t col_o(int t) { return 256u + 128u * (uint32_t)t; }
 constexpr float kRescaleLog2 = 8.f;
 
 enum Bar : int {
   kQFull = 0,
-  kKvFull = 1,    // +stage
-  kKvEmpty = 3,   // +stage
-  kSFull = 5,     // +buffer
-  kSFree = 7,     // +buffer
-  kPFull = 9,     // +buffer
-  kPvDone = 11,   // +buffer
-  kFinal = 13,    // last MMA commit before TMEM is released
-  kNumBars = 14,
+  kKvFull = 1,   // +stage
+  kKvEmpty = 3,  // +stage
+  kSFull = 5,    // +tile
+  kPFull = 7,    // +tile
+  kPvDone = 9,   // +tile
+  kFinal = 11,   // last MMA commit before TMEM is released
+  kNumBars = 12,
 };
 
 struct PrefillParams {
@@ -85,7 +94,7 @@ struct PrefillParams {
   float scale_log2;
   const int64_t* ctrl;
   int32_t* cursor;
-  const int64_t* unit_prefix;  // per request: first prefill unit (query tile)
+  const int64_t* unit_prefix;  // per request: first prefill unit (query-tile pair)
   const int32_t* unit_req;     // unit -> request
   int32_t* status;
 };
@@ -111,12 +120,8 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-struct Item {
-  int64_t r, q0, q1, kbase, kv_lo, kv_hi;  // kv_[lo,hi] inclusive over the tile's rows
-  int32_t h, n;                            // KV head, number of 128-key tiles
-  bool empty_history;
-};
-
+// 10 warps: the busiest SM sub-partition holds 3 of them, so a thread may
+// use at most 168 registers (16 K registers per sub-partition).
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -129,8 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t page_ok_sh[kStages];
   __shared__ int32_t abort_sh;
   __shared__ int32_t last_issued[kStages];  // last KV tile index issued per stage
-  __shared__ int32_t q_issued;              // Q loads issued (phase count of kQFull)
+  __shared__ int32_t q_issued;              // Q loads issued (phases of kQFull)
 
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n_items = p.ctrl[kCtrlPrefillUnits] * p.num_kv_heads;
 
@@ -146,11 +152,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(bar(kQFull), 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar(kKvFull + s), 1);
       mbar_init(bar(kKvEmpty + s), 1);
       mbar_init(bar(kSFull + s), 1);
-      mbar_init(bar(kSFree + s), 4);
       mbar_init(bar(kPFull + s), 4);
       mbar_init(bar(kPvDone + s), 1);
     }
@@ -166,34 +171,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
 
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t idesc_qk = f16_idesc(kBf16, false, kRows, kKeys);
   const uint32_t idesc_pv = f16_idesc(kBf16, true, kRows, 128);
 
-  uint32_t kvc = 0;       // KV tiles consumed so far by this CTA (ring / buffer phases)
-  uint32_t item_cnt = 0;  // items processed (Q barrier phase)
+  // Running counts (identical in every role): KV tiles of this CTA (ring
+  // phases), tiles processed per query tile (S/P/PV phases), Q loads.
+  uint32_t kvc = 0, tc0 = 0, tc1 = 0, qc = 0;
+  // Softmax role of this warp: tile 0 (A) for warps 2-5, 1 (B) for 6-9.
+  const int x = warp >= 6 ? 1 : 0;
+  const int row = 32 * (warp & 3) + lane;  // TMEM lane of this thread
 
   for (;;) {
     const int64_t claimed = item_sh;
     if (claimed >= n_items) break;
     // ---- describe the item (heaviest query tiles first) ----
     const int64_t it = n_items - 1 - claimed;
-    Item I;
-    I.h = (int32_t)(it % p.num_kv_heads);
+    const int h = (int)(it % p.num_kv_heads);
     const int64_t unit = it / p.num_kv_heads;
-    I.r = __ldg(p.unit_req + unit);
-    const int64_t qt = unit - __ldg(p.unit_prefix + I.r);
-    const int64_t qs = __ldg(p.qsl + I.r), qe = __ldg(p.qsl + I.r + 1);
-    I.q0 = qs + qt * p.block_q;
-    I.q1 = min(I.q0 + (int64_t)p.block_q, qe);
+    const int64_t r = __ldg(p.unit_req + unit);
+    const int64_t qt = unit - __ldg(p.unit_prefix + r);
+    const int64_t qs = __ldg(p.qsl + r), qe = __ldg(p.qsl + r + 1);
+    const int64_t q0 = qs + qt * 2 * p.block_q;  // first token of tile A
+    const bool b_active = q0 + p.block_q < qe;
     const int64_t gather_lo = max(__ldg(p.qstart + qs), (int64_t)0);
-    const int64_t clen = __ldg(p.ctx_len + I.r);
-    I.empty_history = clen <= gather_lo;
+    const int64_t clen = __ldg(p.ctx_len + r);
+    const bool empty_history = clen <= gather_lo;
 
     // Per-row visibility window (softmax threads own rows).
-    const int row = 32 * (warp & 3) + lane;
-    const int64_t tok = I.q0 + row / p.group;
-    const bool row_valid = warp >= 2 && tok < I.q1;
+    const int64_t tok = q0 + (int64_t)x * p.block_q + row / p.group;
+    const bool row_valid = warp >= 2 && tok < min(qe, q0 + (int64_t)(x + 1) * p.block_q);
     int64_t lo_q = 1, hi_q = 0;
     if (row_valid) {
       lo_q = max(gather_lo, __ldg(p.qstart + tok));
@@ -210,205 +216,210 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     const bool any = kv_hi_sh > 0ull && kv_lo_sh != ~0ull;
-    I.kv_lo = any ? (int64_t)kv_lo_sh : 0;
-    I.kv_hi = any ? (int64_t)kv_hi_sh - 1 : -1;
-    I.kbase = I.kv_lo & ~(int64_t)15;
-    I.n = any ? (int32_t)((I.kv_hi - I.kbase) / kKeys + 1) : 0;
-    const int64_t* trow = p.table + I.r * p.table_stride;
+    const int64_t kv_lo = any ? (int64_t)kv_lo_sh : 0;
+    const int64_t kv_hi = any ? (int64_t)kv_hi_sh - 1 : -1;
+    const int64_t kbase = kv_lo & ~(int64_t)15;
+    const int n = any ? (int)((kv_hi - kbase) / kKeys + 1) : 0;
+    const int64_t* trow = p.table + r * p.table_stride;
+    const int ntiles = b_active ? 2 : 1;
 
-    if (I.n > 0) {
+    if (n > 0) {
       if (warp == 0) {
         // ------------------------------------------------ producer
         if (lane == 0) {
-          mbar_expect_tx(bar(kQFull), kTileBytes);
-          const int32_t qy = I.h * p.group, qz = (int32_t)I.q0;
-          tma_load_3d(sb + kOffQ, &qmap, 0, qy, qz, bar(kQFull));
-          tma_load_3d(sb + kOffQ + kHalf, &qmap, 64, qy, qz, bar(kQFull));
-          q_issued = (int32_t)item_cnt + 1;
+          mbar_expect_tx(bar(kQFull), ntiles * kTileBytes);
+          for (int t = 0; t < ntiles; ++t) {
+            const int32_t qy = h * p.group, qz = (int32_t)(q0 + (int64_t)t * p.block_q);
+            tma_load_3d(sb + kOffQ + t * kTileBytes, &qmap, 0, qy, qz, bar(kQFull));
+            tma_load_3d(sb + kOffQ + t * kTileBytes + kHalf, &qmap, 64, qy, qz, bar(kQFull));
+          }
+          q_issued = (int32_t)qc + 1;
         }
-        for (int j = 0; j < I.n; ++j) {
+        for (int j = 0; j < n; ++j) {
           const uint32_t c = kvc + j, s = c & 1, ph = (c >> 1) & 1;
           if (!mbar_wait(bar(kKvEmpty + s), ph ^ 1)) {
             if (lane == 0) atomicOr(&abort_sh, 1);
             break;
           }
-          const int64_t pos = I.kbase + (int64_t)j * kKeys + 16 * lane;
+          const int64_t pos = kbase + (int64_t)j * kKeys + 16 * lane;
           int64_t blk = -1;
           if (lane < 8) blk = page_of(p, trow, pos);
           const bool ok = blk >= 0;
           const uint32_t mask = __ballot_sync(0xffffffffu, ok) & 0xffu;
           if (lane == 0) {
             page_ok_sh[s] = mask;
+            last_issued[s] = (int32_t)c;
             mbar_expect_tx(bar(kKvFull + s), kStageBytes);
           }
           __syncwarp();
-          if (lane == 0) last_issued[s] = (int32_t)c;
           if (lane < 8) {
             const int64_t page = ok ? blk : 0;
             const int64_t off = p.bs_shift >= 0 ? (pos & (p.block_size - 1)) : pos % p.block_size;
             const int32_t y = (int32_t)(page * p.block_size + off);
-            const int32_t x = I.h * 128;
+            const int32_t xk = h * 128;
             const uint32_t k_dst = sb + kOffKv + s * kStageBytes + lane * 2048;
             const uint32_t v_dst = k_dst + kTileBytes;
-            tma_load_2d(k_dst, &kvmap, x, y, bar(kKvFull + s));
-            tma_load_2d(k_dst + kHalf, &kvmap, x + 64, y, bar(kKvFull + s));
-            tma_load_2d(v_dst, &kvmap, x, y + (int32_t)p.num_slots, bar(kKvFull + s));
-            tma_load_2d(v_dst + kHalf, &kvmap, x + 64, y + (int32_t)p.num_slots, bar(kKvFull + s));
+            tma_load_2d(k_dst, &kvmap, xk, y, bar(kKvFull + s));
+            tma_load_2d(k_dst + kHalf, &kvmap, xk + 64, y, bar(kKvFull + s));
+            tma_load_2d(v_dst, &kvmap, xk, y + (int32_t)p.num_slots, bar(kKvFull + s));
+            tma_load_2d(v_dst + kHalf, &kvmap, xk + 64, y + (int32_t)p.num_slots, bar(kKvFull + s));
           }
         }
       } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-          bool ok = mbar_wait(bar(kQFull), item_cnt & 1);
-          tc_fence_after();
-          for (int j = 0; ok && j <= I.n; ++j) {
-            if (j < I.n) {
-              const uint32_t c = kvc + j, s = c & 1, ph = (c >> 1) & 1;
-              ok = mbar_wait(bar(kKvFull + s), ph) && mbar_wait(bar(kSFree + s), ph ^ 1);
-              if (!ok) break;
-              tc_fence_after();
-              const uint32_t kb = sb + kOffKv + s * kStageBytes;
+          auto issue_s = [&](int t, uint32_t stage) {
+            const uint32_t kb = sb + kOffKv + stage * kStageBytes;
+            const uint32_t qb = sb + kOffQ + t * kTileBytes;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
+              umma_f16(tmem + col_s(t), sw128_desc(qb + off, 16, 1024),
+                       sw128_desc(kb + off, 16, 1024), idesc_qk, k > 0);
+            }
+            umma_commit(bar(kSFull + t));
+          };
+          auto issue_pv = [&](int t, uint32_t stage, bool acc) {
+            const uint32_t vb = sb + kOffKv + stage * kStageBytes + kTileBytes;
+#pragma unroll
+            for (int part = 0; part < (kBf16 ? 2 : 1); ++part) {  // P_hi (+ P_lo in bf16)
 #pragma unroll
               for (int k = 0; k < 8; ++k) {
-                const uint32_t off = (k >> 2) * kHalf + (k & 3) * 32;
-                umma_f16(tmem + s * kKeys, sw128_desc(sb + kOffQ + off, 16, 1024),
-                         sw128_desc(kb + off, 16, 1024), idesc_qk, k > 0);
+                const uint32_t pcol = col_s(t) + 32 * (k >> 1) + 8 * (k & 1) + 16 * part;
+                umma_f16_ts(tmem + col_o(t), tmem + pcol, sw128_desc(vb + k * 2048, kHalf, 1024),
+                            idesc_pv, acc || k > 0 || part > 0);
               }
-              umma_commit(bar(kSFull + s));
             }
-            if (j >= 1) {
-              const uint32_t c = kvc + j - 1, s = c & 1, ph = (c >> 1) & 1;
-              ok = mbar_wait(bar(kPFull + s), ph);
+            umma_commit(bar(kPvDone + t));
+          };
+          bool ok = mbar_wait(bar(kQFull), qc & 1) &&
+                    mbar_wait(bar(kKvFull + (kvc & 1)), (kvc >> 1) & 1);
+          if (ok) {
+            tc_fence_after();
+            for (int t = 0; t < ntiles; ++t) issue_s(t, kvc & 1);
+          }
+          for (int j = 0; ok && j < n; ++j) {
+            const uint32_t c = kvc + j, s = c & 1;
+            const uint32_t cn = c + 1, sn = cn & 1;
+            for (int t = 0; t < ntiles; ++t) {
+              ok = mbar_wait(bar(kPFull + t), ((t == 0 ? tc0 : tc1) + j) & 1);
               if (!ok) break;
               tc_fence_after();
-              const uint32_t vb = sb + kOffKv + s * kStageBytes + kTileBytes;
-#pragma unroll
-              for (int part = 0; part < (kBf16 ? 2 : 1); ++part) {  // P_hi (+ P_lo in bf16)
-                const uint32_t pb = sb + kOffP + part * kTileBytes;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                  umma_f16(tmem + kTmemO,
-                           sw128_desc(pb + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024),
-                           sw128_desc(vb + k * 2048, kHalf, 1024), idesc_pv,
-                           (j > 1) || (k > 0) || (part > 0));
+              issue_pv(t, s, j > 0);
+              if (t == ntiles - 1) umma_commit(bar(kKvEmpty + s));  // K_j, V_j fully consumed
+              if (j + 1 < n) {
+                if (t == 0) {
+                  ok = mbar_wait(bar(kKvFull + sn), (cn >> 1) & 1);
+                  if (!ok) break;
+                  tc_fence_after();
                 }
+                issue_s(t, sn);
               }
-              umma_commit(bar(kKvEmpty + s));
-              umma_commit(bar(kPvDone + s));
             }
           }
           if (!ok) atomicOr(&abort_sh, 1);
         }
         __syncwarp();
-      } else {
-        // ------------------------------------------------ softmax / epilogue
+      } else if (x == 0 || b_active) {
+        // ------------------------------------------------ softmax / epilogue of tile x
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const uint32_t s_cols = tmem + lane_base + col_s(x);
+        const uint32_t o_cols = tmem + lane_base + col_o(x);
+        const uint32_t tcx = x == 0 ? tc0 : tc1;
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < I.n; ++j) {
-          const uint32_t c = kvc + j, s = c & 1, ph = (c >> 1) & 1;
-          ok = mbar_wait(bar(kSFull + s), ph) && mbar_wait(bar(kKvFull + s), ph);
+        for (int j = 0; j < n; ++j) {
+          const uint32_t c = kvc + j, s = c & 1;
+          ok = mbar_wait(bar(kSFull + x), (tcx + j) & 1) &&
+               mbar_wait(bar(kKvFull + s), (c >> 1) & 1);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          float sv[kKeys];
-#pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            float tmp[32];
-            tmem_ld32(tmem + lane_base + s * kKeys + 32 * ch, tmp);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) sv[32 * ch + i] = tmp[i];
-          }
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kSFree + s));
-
-          const int64_t k0 = I.kbase + (int64_t)j * kKeys;
+          const int64_t k0 = kbase + (int64_t)j * kKeys;
           const uint32_t pok = page_ok_sh[s];
-          const bool whole = row_valid && k0 >= lo_q && k0 + kKeys - 1 <= hi_q && pok == 0xffu;
-          float tmax = -INFINITY;
-          if (whole) {
+          // All 128 scores of this row in one batch of TMEM loads.
+          uint32_t sc[4][32];
 #pragma unroll
-            for (int i = 0; i < kKeys; ++i) {
-              sv[i] *= p.scale_log2;
-              tmax = fmaxf(tmax, sv[i]);
-            }
+          for (int ch = 0; ch < 4; ++ch) tmem_ld32_raw(s_cols + 32 * ch, sc[ch]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) reg_fence(sc[ch]);
+          // Visible keys of this row inside the tile: [lo_rel, hi_rel) on
+          // valid pages.  Hidden scores become -inf once, here.
+          int lo_rel = 0, hi_rel = 0;
+          if (row_valid) {
+            lo_rel = (int)min(max(lo_q - k0, (int64_t)0), (int64_t)kKeys);
+            hi_rel = (int)min(max(hi_q - k0 + 1, (int64_t)0), (int64_t)kKeys);
+          }
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          if (lo_rel == 0 && hi_rel == kKeys && pok == 0xffu) {
+#pragma unroll
+            for (int i = 0; i < kKeys; ++i)
+              mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sc[i >> 5][i & 31]));
           } else {
 #pragma unroll
             for (int i = 0; i < kKeys; ++i) {
-              const int64_t key = k0 + i;
-              const bool vis = row_valid && key >= lo_q && key <= hi_q && ((pok >> (i >> 4)) & 1u);
-              sv[i] = vis ? sv[i] * p.scale_log2 : -INFINITY;
-              tmax = fmaxf(tmax, sv[i]);
+              const bool vis = i >= lo_rel && i < hi_rel && ((pok >> (i >> 4)) & 1u);
+              const float v = vis ? __uint_as_float(sc[i >> 5][i & 31]) : -INFINITY;
+              sc[i >> 5][i & 31] = __float_as_uint(v);
+              mx[i & 3] = fmaxf(mx[i & 3], v);
             }
           }
+          // scale > 0, so the max of the scaled scores is the scaled max.
+          const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
           float corr = 1.f;
           if (tmax > m_ref + kRescaleLog2) {
-            corr = exp2f(m_ref - tmax);  // 0 when m_ref is -inf
+            corr = ex2(m_ref - tmax);  // 0 when m_ref is -inf
             l *= corr;
             m_ref = tmax;
           }
-          // PV_{j-1} done: O may be rescaled and the P buffer it read is free.
-          if (j >= 1) {
-            const uint32_t cp = c - 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(kPvDone + (cp & 1)), (cp >> 1) & 1))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            if (__any_sync(0xffffffffu, corr != 1.f)) {
+          // O holds PV(j-1), complete because S(j) (issued after it) is.
+          if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+            for (int ch = 0; ch < 8; ++ch) {  // 16 columns at a time: the scores stay live
+              uint32_t o[16];
+              tmem_ld16_raw(o_cols + 16 * ch, o);
+              tmem_wait_ld();
+              reg_fence(o);
 #pragma unroll
-              for (int ch = 0; ch < 4; ++ch) {
-                float o[32];
-                tmem_ld32(tmem + lane_base + kTmemO + 32 * ch, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] *= corr;
-                tmem_st32(tmem + lane_base + kTmemO + 32 * ch, o);
-              }
-              tmem_wait_st();
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+              tmem_st16(o_cols + 16 * ch, o);
             }
           }
+          // P = 2^(s*scale - m_ref), written over S as packed 16-bit pairs:
+          // keys 32ch..32ch+31 -> columns 32ch..32ch+15 (P_hi) and
+          // 32ch+16..32ch+31 (P_lo, bf16 only), behind the scores already read.
           const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-          float psum = 0.f;
-          // P goes to the A operand of the P.V MMA.  In bf16 (8-bit mantissa)
-          // it is split into P_hi + P_lo, both bf16, so P keeps ~16 bits and
-          // the two MMAs into O match the fp16 path's accuracy.
-          uint8_t* prow = smem + kOffP + row * 128;
+          float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-              uint32_t w[4], wl[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = half * 64 + cc * 8 + 2 * e;
-                const float a = exp2f(sv[i] - mu), b = exp2f(sv[i + 1] - mu);
-                psum += a + b;
-                w[e] = pack2<T>(a, b);
-                if constexpr (kBf16) {
-                  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
-                  const float2 hf = __bfloat1622float2(hi);
-                  wl[e] = pack2<T>(a - hf.x, b - hf.y);
-                }
+            for (int i = 0; i < 32; i += 2) {
+              const float pa = ex2(fmaf(__uint_as_float(sc[ch][i]), p.scale_log2, -mu));
+              const float pb = ex2(fmaf(__uint_as_float(sc[ch][i + 1]), p.scale_log2, -mu));
+              ps[(i >> 1) & 3] += pa + pb;
+              hi[i >> 1] = pack2<T>(pa, pb);
+              if constexpr (kBf16) {
+                const float2 hf =
+                    __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi[i >> 1]));
+                lo[i >> 1] = pack2<T>(pa - hf.x, pb - hf.y);
               }
-              const int off = half * kHalf + ((cc ^ (row & 7)) << 4);
-              *reinterpret_cast<uint4*>(prow + off) = make_uint4(w[0], w[1], w[2], w[3]);
-              if constexpr (kBf16)
-                *reinterpret_cast<uint4*>(prow + kTileBytes + off) =
-                    make_uint4(wl[0], wl[1], wl[2], wl[3]);
             }
+            tmem_st16(s_cols + 32 * ch, hi);
+            if constexpr (kBf16) tmem_st16(s_cols + 32 * ch + 16, lo);
           }
+          tmem_wait_st();
+          const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
           l += psum;
-          // Zero V rows no query of this tile may see (below the window,
-          // past the last query, or on a missing page): they hold stale or
-          // sentinel bytes that must not reach O as 0 * NaN.
-          {
+          if (x == 0) {
+            // Zero V rows no query of the pair may see (below the window,
+            // past the last query, or on a missing page): they hold stale or
+            // sentinel bytes that must not reach O as 0 * NaN.
             const int64_t key = k0 + row;
-            if (key < I.kv_lo || key > I.kv_hi || !((pok >> (row >> 4)) & 1u)) {
+            if (key < kv_lo || key > kv_hi || !((pok >> (row >> 4)) & 1u)) {
               uint8_t* vrow = smem + kOffKv + s * kStageBytes + kTileBytes + row * 128;
               const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
@@ -417,23 +428,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4*>(vrow + kHalf + cc * 16) = z;
               }
             }
+            fence_proxy_async();
           }
-          fence_proxy_async();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kPFull + s));
+          if (lane == 0) mbar_arrive(bar(kPFull + x));
         }
         // ---- epilogue: O / l -> output rows ----
-        const uint32_t cl = kvc + I.n - 1;
-        if (ok && __all_sync(0xffffffffu, mbar_wait(bar(kPvDone + (cl & 1)), (cl >> 1) & 1))) {
+        if (ok && __all_sync(0xffffffffu, mbar_wait(bar(kPvDone + x), (tcx + n - 1) & 1))) {
           tc_fence_after();
           const float inv = l > 0.f ? 1.f / l : NAN;
           T* orow = reinterpret_cast<T*>(p.out) +
-                    (tok * p.num_q_heads + I.h * p.group + row % p.group) * 128;
+                    (tok * p.num_q_heads + h * p.group + row % p.group) * 128;
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
             float o[32];
-            tmem_ld32(tmem + lane_base + kTmemO + 32 * ch, o);
+            tmem_ld32(o_cols + 32 * ch, o);
             tmem_wait_ld();
             if (row_valid) {
 #pragma unroll
@@ -447,7 +457,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          tc_fence_before();
         } else {
           ok = false;
         }
@@ -456,15 +465,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 2 && row_valid) {
       // No visible key at all: 0 for an empty gathered history, else NaN
       // (softmax over an all -inf row), as the reference.
-      const float v = I.empty_history ? 0.f : NAN;
+      const float v = empty_history ? 0.f : NAN;
       T* orow = reinterpret_cast<T*>(p.out) +
-                (tok * p.num_q_heads + I.h * p.group + row % p.group) * 128;
+                (tok * p.num_q_heads + h * p.group + row % p.group) * 128;
       const uint32_t pv = pack2<T>(v, v);
       for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = make_uint4(pv, pv, pv, pv);
     }
 
-    kvc += (uint32_t)I.n;
-    if (I.n > 0) ++item_cnt;  // kQFull completes one phase per item with work
+    if (n > 0) {
+      kvc += (uint32_t)n;
+      tc0 += (uint32_t)n;
+      if (b_active) tc1 += (uint32_t)n;
+      ++qc;
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -517,6 +530,24 @@ EncodeTiled encoder() {
 
 }  // namespace
 
+int prefill_tokens_per_unit(int32_t group) { return 2 * kRows / group; }
+
+// The kernel's registers allow a 320-thread block on this device.
+bool prefill_kernel_fits() {
+  static int cached_device = -1;
+  static bool fits = false;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_device) {
+    cudaFuncAttributes fa_h, fa_b;
+    fits = cudaFuncGetAttributes(&fa_h, paged_prefill_kernel<__half>) == cudaSuccess &&
+           cudaFuncGetAttributes(&fa_b, paged_prefill_kernel<__nv_bfloat16>) == cudaSuccess &&
+           fa_h.maxThreadsPerBlock >= kThreads && fa_b.maxThreadsPerBlock >= kThreads;
+    cached_device = dev;
+  }
+  return fits;
+}
+
 bool prefill_tc_supported(const AttentionProblem& a) {
   const int group = a.num_q_heads / a.num_kv_heads;
   const int64_t num_slots = a.num_blocks * a.block_size;
@@ -525,7 +556,7 @@ bool prefill_tc_supported(const AttentionProblem& a) {
          ((uintptr_t)a.query % 16) == 0 && ((uintptr_t)a.cache % 16) == 0 &&
          ((uintptr_t)a.out % 16) == 0 && (a.q_st % 8) == 0 && (a.q_sh % 8) == 0 &&
          a.q_sh >= 128 && 2 * num_slots < ((int64_t)1 << 31) && a.num_tokens < ((int64_t)1 << 31) &&
-         encoder() != nullptr;
+         encoder() != nullptr && prefill_kernel_fits();
 }
 
 int launch_paged_prefill(const AttentionProblem& a, const WorkspaceLayout& w) {
