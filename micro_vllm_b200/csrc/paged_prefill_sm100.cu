@@ -4,7 +4,7 @@
 // Work item = (prefill-class request, pair of 128-row query tiles, KV head).
 // Each tile's 128 MMA rows are 128/G query tokens x the G query heads of one
 // GQA group; the two tiles (A: the earlier tokens, B: the next ones) share
-// every K/V tile fetched.  A persistent grid (one CTA per SM, 193 KB of
+// every K/V tile fetched.  A persistent grid (one CTA per SM, 225 KB of
 // shared memory, all 512 TMEM columns) pulls items from an atomic cursor,
 // heaviest (latest) query tiles first.
 //
@@ -14,7 +14,7 @@
 //           rows) and, per 128-key KV tile, the 8 pages of K and V (a 2-D
 //           tensor map over the cache's [2*NB*bs slots, Hkv*128] view; one
 //           16-row x 64-element box per page, plane and half) into a
-//           2-stage ring, 128-byte swizzled — the layout the tensor cores
+//           3-stage K ring and a 2-stage V ring, 128-byte swizzled — the layout the tensor cores
 //           read directly.  Pages missing from the block table are fetched
 //           from page 0 and masked.
 //   warp 1  MMA issuer (one thread), ping-pong between the tiles:
@@ -61,11 +61,12 @@ constexpr int kRows = 128;                   // MMA M: rows of one query tile
 constexpr int kKeys = 128;                   // keys per KV tile
 constexpr int kHalf = kRows * 128;           // [128 rows][64 elem] swizzled half: 16 KiB
 constexpr int kTileBytes = 2 * kHalf;        // [128][128] 16-bit: 32 KiB
-constexpr int kStageBytes = 2 * kTileBytes;  // K + V
-constexpr int kStages = 2;
+constexpr int kKStages = 3;                  // K ring: loads run a full tile ahead
+constexpr int kVStages = 2;                  // V ring
 constexpr int kOffQ = 0;                     // Q_A, Q_B
-constexpr int kOffKv = 2 * kTileBytes;
-constexpr int kSmemUsed = kOffKv + kStages * kStageBytes;  // 192 KiB
+constexpr int kOffK = 2 * kTileBytes;
+constexpr int kOffV = kOffK + kKStages * kTileBytes;
+constexpr int kSmemUsed = kOffV + kVStages * kTileBytes;  // 224 KiB
 constexpr int kSmemBytes = kSmemUsed + 1024;               // + alignment slack
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
@@ -76,14 +77,22 @@ constexpr float kRescaleLog2 = 8.f;
 
 enum Bar : int {
   kQFull = 0,
-  kKvFull = 1,   // +stage
-  kKvEmpty = 3,  // +stage
-  kSFull = 5,    // +tile
-  kPFull = 7,    // +tile
-  kPvDone = 9,   // +tile
-  kFinal = 11,   // last MMA commit before TMEM is released
-  kNumBars = 12,
+  kKFull = 1,    // +K stage: K tile landed
+  kKEmpty = 4,   // +K stage: every S MMA read it
+  kVFull = 7,    // +V stage: V tile landed
+  kVEmpty = 9,   // +V stage: every P.V MMA read it
+  kSFull = 11,   // +tile
+  kPFull = 13,   // +tile
+  kPvDone = 15,  // +tile
+  kFinal = 17,   // last MMA commit before TMEM is released
+  kNumBars = 18,
 };
+
+// Ring slot and phase of the c-th KV tile this CTA processes.
+__device__ __forceinline__ uint32_t kslot(uint32_t c) { return c % kKStages; }
+__device__ __forceinline__ uint32_t kphase(uint32_t c) { return (c / kKStages) & 1; }
+__device__ __forceinline__ uint32_t vslot(uint32_t c) { return c % kVStages; }
+__device__ __forceinline__ uint32_t vphase(uint32_t c) { return (c / kVStages) & 1; }
 
 struct PrefillParams {
   char* out;
@@ -131,9 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int32_t item_sh;
   __shared__ unsigned long long kv_lo_sh, kv_hi_sh;
-  __shared__ uint32_t page_ok_sh[kStages];
   __shared__ int32_t abort_sh;
-  __shared__ int32_t last_issued[kStages];  // last KV tile index issued per stage
+  __shared__ int32_t last_issued[2];  // last K and last V tile index issued
   __shared__ int32_t q_issued;              // Q loads issued (phases of kQFull)
 
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -152,9 +160,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     mbar_init(bar(kQFull), 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(bar(kKFull + s), 1);
+      mbar_init(bar(kKEmpty + s), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(bar(kVFull + s), 1);
+      mbar_init(bar(kVEmpty + s), 1);
+    }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(kKvFull + s), 1);
-      mbar_init(bar(kKvEmpty + s), 1);
       mbar_init(bar(kSFull + s), 1);
       mbar_init(bar(kPFull + s), 4);
       mbar_init(bar(kPvDone + s), 1);
@@ -197,13 +211,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t clen = __ldg(p.ctx_len + r);
     const bool empty_history = clen <= gather_lo;
 
-    // Per-row visibility window (softmax threads own rows).
+    // Per-row visibility window (softmax threads own rows).  Positions fit
+    // 32 bits: the planner refuses contexts longer than 2^30.
     const int64_t tok = q0 + (int64_t)x * p.block_q + row / p.group;
     const bool row_valid = warp >= 2 && tok < min(qe, q0 + (int64_t)(x + 1) * p.block_q);
-    int64_t lo_q = 1, hi_q = 0;
+    int32_t lo_q = 1, hi_q = 0;
     if (row_valid) {
-      lo_q = max(gather_lo, __ldg(p.qstart + tok));
-      hi_q = min(clen - 1, __ldg(p.qpos + tok));
+      lo_q = (int32_t)min(max(gather_lo, __ldg(p.qstart + tok)), kMaxContext);
+      hi_q = (int32_t)max(min(clen - 1, __ldg(p.qpos + tok)), (int64_t)-1);
     }
     if (tid == 0) {
       kv_lo_sh = ~0ull;
@@ -216,10 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     const bool any = kv_hi_sh > 0ull && kv_lo_sh != ~0ull;
-    const int64_t kv_lo = any ? (int64_t)kv_lo_sh : 0;
-    const int64_t kv_hi = any ? (int64_t)kv_hi_sh - 1 : -1;
-    const int64_t kbase = kv_lo & ~(int64_t)15;
-    const int n = any ? (int)((kv_hi - kbase) / kKeys + 1) : 0;
+    const int32_t kv_lo = any ? (int32_t)kv_lo_sh : 0;
+    const int32_t kv_hi = any ? (int32_t)kv_hi_sh - 1 : -1;
+    const int32_t kbase = kv_lo & ~15;
+    const int n = any ? (kv_hi - kbase) / kKeys + 1 : 0;
     const int64_t* trow = p.table + r * p.table_stride;
     const int ntiles = b_active ? 2 : 1;
 
@@ -236,40 +251,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           q_issued = (int32_t)qc + 1;
         }
         for (int j = 0; j < n; ++j) {
-          const uint32_t c = kvc + j, s = c & 1, ph = (c >> 1) & 1;
-          if (!mbar_wait(bar(kKvEmpty + s), ph ^ 1)) {
+          const uint32_t c = kvc + j, sk = kslot(c), sv = vslot(c);
+          // K(j) reuses the stage of K(j-3), free once every S(j-3) MMA ran;
+          // V(j) that of V(j-2), free once every P.V(j-2) MMA ran.
+          if (!mbar_wait(bar(kKEmpty + sk), kphase(c) ^ 1)) {
             if (lane == 0) atomicOr(&abort_sh, 1);
             break;
           }
-          const int64_t pos = kbase + (int64_t)j * kKeys + 16 * lane;
+          const int64_t pos = (int64_t)kbase + (int64_t)j * kKeys + 16 * lane;
           int64_t blk = -1;
           if (lane < 8) blk = page_of(p, trow, pos);
-          const bool ok = blk >= 0;
-          const uint32_t mask = __ballot_sync(0xffffffffu, ok) & 0xffu;
+          const bool ok = blk >= 0;  // missing pages load page 0 (masked by the softmax)
           if (lane == 0) {
-            page_ok_sh[s] = mask;
-            last_issued[s] = (int32_t)c;
-            mbar_expect_tx(bar(kKvFull + s), kStageBytes);
+            last_issued[0] = (int32_t)c;
+            mbar_expect_tx(bar(kKFull + sk), kTileBytes);
+          }
+          __syncwarp();
+          const int64_t page = ok ? blk : 0;
+          const int64_t off = p.bs_shift >= 0 ? (pos & (p.block_size - 1)) : pos % p.block_size;
+          const int32_t y = (int32_t)(page * p.block_size + off);
+          const int32_t xk = h * 128;
+          const uint32_t k_dst = sb + kOffK + sk * kTileBytes + lane * 2048;
+          const uint32_t v_dst = sb + kOffV + sv * kTileBytes + lane * 2048;
+          if (lane < 8) {
+            tma_load_2d(k_dst, &kvmap, xk, y, bar(kKFull + sk));
+            tma_load_2d(k_dst + kHalf, &kvmap, xk + 64, y, bar(kKFull + sk));
+          }
+          if (!mbar_wait(bar(kVEmpty + sv), vphase(c) ^ 1)) {
+            if (lane == 0) atomicOr(&abort_sh, 1);
+            break;
+          }
+          if (lane == 0) {
+            last_issued[1] = (int32_t)c;
+            mbar_expect_tx(bar(kVFull + sv), kTileBytes);
           }
           __syncwarp();
           if (lane < 8) {
-            const int64_t page = ok ? blk : 0;
-            const int64_t off = p.bs_shift >= 0 ? (pos & (p.block_size - 1)) : pos % p.block_size;
-            const int32_t y = (int32_t)(page * p.block_size + off);
-            const int32_t xk = h * 128;
-            const uint32_t k_dst = sb + kOffKv + s * kStageBytes + lane * 2048;
-            const uint32_t v_dst = k_dst + kTileBytes;
-            tma_load_2d(k_dst, &kvmap, xk, y, bar(kKvFull + s));
-            tma_load_2d(k_dst + kHalf, &kvmap, xk + 64, y, bar(kKvFull + s));
-            tma_load_2d(v_dst, &kvmap, xk, y + (int32_t)p.num_slots, bar(kKvFull + s));
-            tma_load_2d(v_dst + kHalf, &kvmap, xk + 64, y + (int32_t)p.num_slots, bar(kKvFull + s));
+            tma_load_2d(v_dst, &kvmap, xk, y + (int32_t)p.num_slots, bar(kVFull + sv));
+            tma_load_2d(v_dst + kHalf, &kvmap, xk + 64, y + (int32_t)p.num_slots, bar(kVFull + sv));
           }
         }
       } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
           auto issue_s = [&](int t, uint32_t stage) {
-            const uint32_t kb = sb + kOffKv + stage * kStageBytes;
+            const uint32_t kb = sb + kOffK + stage * kTileBytes;
             const uint32_t qb = sb + kOffQ + t * kTileBytes;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -280,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(bar(kSFull + t));
           };
           auto issue_pv = [&](int t, uint32_t stage, bool acc) {
-            const uint32_t vb = sb + kOffKv + stage * kStageBytes + kTileBytes;
+            const uint32_t vb = sb + kOffV + stage * kTileBytes;
 #pragma unroll
             for (int part = 0; part < (kBf16 ? 2 : 1); ++part) {  // P_hi (+ P_lo in bf16)
 #pragma unroll
@@ -293,27 +319,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(bar(kPvDone + t));
           };
           bool ok = mbar_wait(bar(kQFull), qc & 1) &&
-                    mbar_wait(bar(kKvFull + (kvc & 1)), (kvc >> 1) & 1);
+                    mbar_wait(bar(kKFull + kslot(kvc)), kphase(kvc));
           if (ok) {
             tc_fence_after();
-            for (int t = 0; t < ntiles; ++t) issue_s(t, kvc & 1);
+            for (int t = 0; t < ntiles; ++t) issue_s(t, kslot(kvc));
+            umma_commit(bar(kKEmpty + kslot(kvc)));  // K(0) read by every S(0)
           }
           for (int j = 0; ok && j < n; ++j) {
-            const uint32_t c = kvc + j, s = c & 1;
-            const uint32_t cn = c + 1, sn = cn & 1;
+            const uint32_t c = kvc + j, sv = vslot(c);
+            const uint32_t cn = c + 1, skn = kslot(cn);
             for (int t = 0; t < ntiles; ++t) {
               ok = mbar_wait(bar(kPFull + t), ((t == 0 ? tc0 : tc1) + j) & 1);
+              if (ok && t == 0) ok = mbar_wait(bar(kVFull + sv), vphase(c));
               if (!ok) break;
               tc_fence_after();
-              issue_pv(t, s, j > 0);
-              if (t == ntiles - 1) umma_commit(bar(kKvEmpty + s));  // K_j, V_j fully consumed
+              issue_pv(t, sv, j > 0);
+              if (t == ntiles - 1) umma_commit(bar(kVEmpty + sv));  // V(j) read by every P.V(j)
               if (j + 1 < n) {
                 if (t == 0) {
-                  ok = mbar_wait(bar(kKvFull + sn), (cn >> 1) & 1);
+                  ok = mbar_wait(bar(kKFull + skn), kphase(cn));
                   if (!ok) break;
                   tc_fence_after();
                 }
-                issue_s(t, sn);
+                issue_s(t, skn);
+                if (t == ntiles - 1) umma_commit(bar(kKEmpty + skn));  // K(j+1) read by every S
               }
             }
           }
@@ -329,16 +358,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < n; ++j) {
-          const uint32_t c = kvc + j, s = c & 1;
-          ok = mbar_wait(bar(kSFull + x), (tcx + j) & 1) &&
-               mbar_wait(bar(kKvFull + s), (c >> 1) & 1);
+          const uint32_t c = kvc + j, sv = vslot(c);
+          const int32_t k0 = kbase + j * kKeys;
+          // Pages of this KV tile that exist in the block table (lanes 0-7
+          // look up one 16-key page each; loaded before the wait).
+          uint32_t pok;
+          {
+            int64_t blk = -1;
+            if (lane < 8) blk = page_of(p, trow, (int64_t)k0 + 16 * lane);
+            pok = __ballot_sync(0xffffffffu, blk >= 0) & 0xffu;
+          }
+          ok = mbar_wait(bar(kSFull + x), (tcx + j) & 1);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int64_t k0 = kbase + (int64_t)j * kKeys;
-          const uint32_t pok = page_ok_sh[s];
           // All 128 scores of this row in one batch of TMEM loads.
           uint32_t sc[4][32];
 #pragma unroll
@@ -350,8 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // valid pages.  Hidden scores become -inf once, here.
           int lo_rel = 0, hi_rel = 0;
           if (row_valid) {
-            lo_rel = (int)min(max(lo_q - k0, (int64_t)0), (int64_t)kKeys);
-            hi_rel = (int)min(max(hi_q - k0 + 1, (int64_t)0), (int64_t)kKeys);
+            lo_rel = min(max(lo_q - k0, 0), kKeys);
+            hi_rel = min(max(hi_q - k0 + 1, 0), kKeys);
           }
           float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
           if (lo_rel == 0 && hi_rel == kKeys && pok == 0xffu) {
@@ -395,21 +430,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
-            uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float pa = ex2(fmaf(__uint_as_float(sc[ch][i]), p.scale_log2, -mu));
-              const float pb = ex2(fmaf(__uint_as_float(sc[ch][i + 1]), p.scale_log2, -mu));
-              ps[(i >> 1) & 3] += pa + pb;
-              hi[i >> 1] = pack2<T>(pa, pb);
-              if constexpr (kBf16) {
-                const float2 hf =
-                    __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi[i >> 1]));
-                lo[i >> 1] = pack2<T>(pa - hf.x, pb - hf.y);
+            for (int hh = 0; hh < 2; ++hh) {  // 16 keys: 8 packed columns per store
+              uint32_t hi[8], lo[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int i = 16 * hh + 2 * e;
+                const float pa = ex2(fmaf(__uint_as_float(sc[ch][i]), p.scale_log2, -mu));
+                const float pb = ex2(fmaf(__uint_as_float(sc[ch][i + 1]), p.scale_log2, -mu));
+                ps[e & 3] += pa + pb;
+                hi[e] = pack2<T>(pa, pb);
+                if constexpr (kBf16) {
+                  const float2 hf =
+                      __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi[e]));
+                  lo[e] = pack2<T>(pa - hf.x, pb - hf.y);
+                }
               }
+              tmem_st8(s_cols + 32 * ch + 8 * hh, hi);
+              if constexpr (kBf16) tmem_st8(s_cols + 32 * ch + 16 + 8 * hh, lo);
             }
-            tmem_st16(s_cols + 32 * ch, hi);
-            if constexpr (kBf16) tmem_st16(s_cols + 32 * ch + 16, lo);
           }
           tmem_wait_st();
           const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
@@ -418,9 +457,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Zero V rows no query of the pair may see (below the window,
             // past the last query, or on a missing page): they hold stale or
             // sentinel bytes that must not reach O as 0 * NaN.
-            const int64_t key = k0 + row;
+            const int32_t key = k0 + row;
             if (key < kv_lo || key > kv_hi || !((pok >> (row >> 4)) & 1u)) {
-              uint8_t* vrow = smem + kOffKv + s * kStageBytes + kTileBytes + row * 128;
+              // V(j) must have landed before its rows are overwritten.
+              if (!mbar_wait(bar(kVFull + sv), vphase(c))) atomicOr(&abort_sh, 1);
+              uint8_t* vrow = smem + kOffV + sv * kTileBytes + row * 128;
               const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
               for (int cc = 0; cc < 8; ++cc) {
@@ -497,8 +538,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(bar(kFinal), 0);
   }
   if (tid == 0 && abort_sh) {
-    for (int s = 0; s < kStages; ++s)
-      if (last_issued[s] >= 0) mbar_wait(bar(kKvFull + s), (last_issued[s] >> 1) & 1);
+    // The last K and V loads issued complete after every earlier one.
+    if (last_issued[0] >= 0) {
+      const uint32_t c = (uint32_t)last_issued[0];
+      mbar_wait(bar(kKFull + kslot(c)), kphase(c));
+    }
+    if (last_issued[1] >= 0) {
+      const uint32_t c = (uint32_t)last_issued[1];
+      mbar_wait(bar(kVFull + vslot(c)), vphase(c));
+    }
     if (q_issued > 0) mbar_wait(bar(kQFull), (q_issued - 1) & 1);
   }
   tc_fence_before();
