@@ -8,13 +8,13 @@
 // shared memory, all 512 TMEM columns) pulls items from an atomic cursor,
 // heaviest (latest) query tiles first.
 //
-// Roles inside a CTA (10 warps):
-//   warp 0  TMA producer: both Q tiles once per item (a 3-D tensor map over
+// Roles inside a CTA (11 warps):
+//   warps 0, 10  TMA producers (K with Q, and V): both Q tiles once per item (a 3-D tensor map over
 //           [token, head, dim] so the G heads of a token land in adjacent
 //           rows) and, per 128-key KV tile, the 8 pages of K and V (a 2-D
 //           tensor map over the cache's [2*NB*bs slots, Hkv*128] view; one
 //           16-row x 64-element box per page, plane and half) into a
-//           3-stage K ring and a 2-stage V ring, 128-byte swizzled — the layout the tensor cores
+//           2-stage K ring and a 3-stage V ring, 128-byte swizzled — the layout the tensor cores
 //           read directly.  Pages missing from the block table are fetched
 //           from page 0 and masked.
 //   warp 1  MMA issuer (one thread), ping-pong between the tiles:
@@ -61,32 +61,34 @@ constexpr int kRows = 128;                   // MMA M: rows of one query tile
 constexpr int kKeys = 128;                   // keys per KV tile
 constexpr int kHalf = kRows * 128;           // [128 rows][64 elem] swizzled half: 16 KiB
 constexpr int kTileBytes = 2 * kHalf;        // [128][128] 16-bit: 32 KiB
-constexpr int kKStages = 3;                  // K ring: loads run a full tile ahead
-constexpr int kVStages = 2;                  // V ring
+constexpr int kKStages = 2;                  // K ring (released right after the S MMAs)
+constexpr int kVStages = 3;                  // V ring (released after the P.V MMAs)
 constexpr int kOffQ = 0;                     // Q_A, Q_B
 constexpr int kOffK = 2 * kTileBytes;
 constexpr int kOffV = kOffK + kKStages * kTileBytes;
 constexpr int kSmemUsed = kOffV + kVStages * kTileBytes;  // 224 KiB
 constexpr int kSmemBytes = kSmemUsed + 1024;               // + alignment slack
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: S/P of tile A and B, then O of tile A and B.
 __device__ __forceinline__ uint32_t col_s(int t) { return 128u * (uint32_t)t; }
 __device__ __forceinline__ uint32_t col_o(int t) { return 256u + 128u * (uint32_t)t; }
 constexpr float kRescaleLog2 = 8.f;
 
+// mbarrier indices, derived from the ring depths so no two overlap.
 enum Bar : int {
   kQFull = 0,
-  kKFull = 1,    // +K stage: K tile landed
-  kKEmpty = 4,   // +K stage: every S MMA read it
-  kVFull = 7,    // +V stage: V tile landed
-  kVEmpty = 9,   // +V stage: every P.V MMA read it
-  kSFull = 11,   // +tile
-  kPFull = 13,   // +tile
-  kPvDone = 15,  // +tile
-  kFinal = 17,   // last MMA commit before TMEM is released
-  kNumBars = 18,
+  kKFull = kQFull + 1,           // +K slot: K tile landed
+  kKEmpty = kKFull + kKStages,   // +K slot: every S MMA read it
+  kVFull = kKEmpty + kKStages,   // +V slot: V tile landed
+  kVEmpty = kVFull + kVStages,   // +V slot: every P.V MMA read it
+  kSFull = kVEmpty + kVStages,   // +tile (A, B)
+  kPFull = kSFull + 2,           // +tile
+  kPvDone = kPFull + 2,          // +tile
+  kFinal = kPvDone + 2,          // last MMA commit before TMEM is released
+  kNumBars = kFinal + 1,
 };
+static_assert(kNumBars == 1 + 2 * kKStages + 2 * kVStages + 3 * 2 + 1, "mbarrier layout");
 
 // Ring slot and phase of the c-th KV tile this CTA processes.
 __device__ __forceinline__ uint32_t kslot(uint32_t c) { return c % kKStages; }
@@ -129,7 +131,7 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 10 warps: the busiest SM sub-partition holds 3 of them, so a thread may
+// 11 warps: the busiest SM sub-partition holds 3 of them, so a thread may
 // use at most 168 registers (16 K registers per sub-partition).
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -214,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Per-row visibility window (softmax threads own rows).  Positions fit
     // 32 bits: the planner refuses contexts longer than 2^30.
     const int64_t tok = q0 + (int64_t)x * p.block_q + row / p.group;
-    const bool row_valid = warp >= 2 && tok < min(qe, q0 + (int64_t)(x + 1) * p.block_q);
+    const bool row_valid =
+        warp >= 2 && warp < 10 && tok < min(qe, q0 + (int64_t)(x + 1) * p.block_q);
     int32_t lo_q = 1, hi_q = 0;
     if (row_valid) {
       lo_q = (int32_t)min(max(gather_lo, __ldg(p.qstart + tok)), kMaxContext);
@@ -239,9 +242,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ntiles = b_active ? 2 : 1;
 
     if (n > 0) {
-      if (warp == 0) {
-        // ------------------------------------------------ producer
-        if (lane == 0) {
+      if (warp == 0 || warp == 10) {
+        // ------------------------------------------------ producers
+        // Warp 0 loads Q and the K tiles, warp 10 the V tiles; each waits
+        // only on its own ring, so K is never held up behind a V slot.
+        const bool is_k = warp == 0;
+        if (is_k && lane == 0) {
           mbar_expect_tx(bar(kQFull), ntiles * kTileBytes);
           for (int t = 0; t < ntiles; ++t) {
             const int32_t qy = h * p.group, qz = (int32_t)(q0 + (int64_t)t * p.block_q);
@@ -251,44 +257,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           q_issued = (int32_t)qc + 1;
         }
         for (int j = 0; j < n; ++j) {
-          const uint32_t c = kvc + j, sk = kslot(c), sv = vslot(c);
-          // K(j) reuses the stage of K(j-3), free once every S(j-3) MMA ran;
-          // V(j) that of V(j-2), free once every P.V(j-2) MMA ran.
-          if (!mbar_wait(bar(kKEmpty + sk), kphase(c) ^ 1)) {
+          const uint32_t c = kvc + j;
+          const uint32_t slot = is_k ? kslot(c) : vslot(c);
+          const uint32_t full = bar((is_k ? kKFull : kVFull) + slot);
+          // K(j) reuses the slot of K(j-2), free once every S(j-2) MMA ran;
+          // V(j) that of V(j-3), free once every P.V(j-3) MMA ran.
+          const uint32_t empty_phase = (is_k ? kphase(c) : vphase(c)) ^ 1;
+          if (!mbar_wait(bar((is_k ? kKEmpty : kVEmpty) + slot), empty_phase)) {
             if (lane == 0) atomicOr(&abort_sh, 1);
             break;
           }
           const int64_t pos = (int64_t)kbase + (int64_t)j * kKeys + 16 * lane;
           int64_t blk = -1;
           if (lane < 8) blk = page_of(p, trow, pos);
-          const bool ok = blk >= 0;  // missing pages load page 0 (masked by the softmax)
           if (lane == 0) {
-            last_issued[0] = (int32_t)c;
-            mbar_expect_tx(bar(kKFull + sk), kTileBytes);
-          }
-          __syncwarp();
-          const int64_t page = ok ? blk : 0;
-          const int64_t off = p.bs_shift >= 0 ? (pos & (p.block_size - 1)) : pos % p.block_size;
-          const int32_t y = (int32_t)(page * p.block_size + off);
-          const int32_t xk = h * 128;
-          const uint32_t k_dst = sb + kOffK + sk * kTileBytes + lane * 2048;
-          const uint32_t v_dst = sb + kOffV + sv * kTileBytes + lane * 2048;
-          if (lane < 8) {
-            tma_load_2d(k_dst, &kvmap, xk, y, bar(kKFull + sk));
-            tma_load_2d(k_dst + kHalf, &kvmap, xk + 64, y, bar(kKFull + sk));
-          }
-          if (!mbar_wait(bar(kVEmpty + sv), vphase(c) ^ 1)) {
-            if (lane == 0) atomicOr(&abort_sh, 1);
-            break;
-          }
-          if (lane == 0) {
-            last_issued[1] = (int32_t)c;
-            mbar_expect_tx(bar(kVFull + sv), kTileBytes);
+            last_issued[is_k ? 0 : 1] = (int32_t)c;
+            mbar_expect_tx(full, kTileBytes);
           }
           __syncwarp();
           if (lane < 8) {
-            tma_load_2d(v_dst, &kvmap, xk, y + (int32_t)p.num_slots, bar(kVFull + sv));
-            tma_load_2d(v_dst + kHalf, &kvmap, xk + 64, y + (int32_t)p.num_slots, bar(kVFull + sv));
+            // Missing pages load page 0; the softmax masks their keys.
+            const int64_t page = blk >= 0 ? blk : 0;
+            const int64_t off = p.bs_shift >= 0 ? (pos & (p.block_size - 1)) : pos % p.block_size;
+            const int32_t y = (int32_t)(page * p.block_size + off) + (is_k ? 0 : (int32_t)p.num_slots);
+            const int32_t xk = h * 128;
+            const uint32_t dst = sb + (is_k ? kOffK : kOffV) + slot * kTileBytes + lane * 2048;
+            tma_load_2d(dst, &kvmap, xk, y, full);
+            tma_load_2d(dst + kHalf, &kvmap, xk + 64, y, full);
           }
         }
       } else if (warp == 1) {
@@ -580,7 +575,7 @@ EncodeTiled encoder() {
 
 int prefill_tokens_per_unit(int32_t group) { return 2 * kRows / group; }
 
-// The kernel's registers allow a 320-thread block on this device.
+// The kernel's registers allow a full 352-thread block on this device.
 bool prefill_kernel_fits() {
   static int cached_device = -1;
   static bool fits = false;
