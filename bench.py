@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--dtype fp16|bf16] [--ctx uniform|fixed4096]
+                    [--workload decode|llama8b|mixed]
 
 Workload (Qwen3-0.6B attention shape): 256 decode
 sequences per GPU, context lengths uniform in [512, 4096] (or all 4096),
@@ -21,6 +22,12 @@ sum(ctx) * Hkv * D * 2 (K and V) * elsize + Q and O (2 * B * Hq * D * elsize)
 ``--impl reference`` times the reference algorithm on the host CPU (the
 numpy port in oracle/, all host threads) on a bounded sample of the same
 workload and reports the same metric.
+
+Other workloads (parity and supplementary lines, not the default):
+``--workload llama8b`` is BASELINE config 4 (32/8 heads, 64 seqs/GPU, ctx
+U[4096,8192], bf16) with the same metric; ``--workload mixed`` is config 3
+(8 chunked prefills of 2048 tokens over cached prefixes + 120 decodes, bf16)
+and reports the prefill kernel's tensor throughput in TFLOP/s.
 """
 
 from __future__ import annotations
@@ -42,6 +49,42 @@ sys.path.insert(0, str(ROOT))
 NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM, BLOCK_SIZE = 16, 8, 128, 16
 BATCH_PER_GPU = 256
 POOL_FRACTION = 0.8
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one paged_decode_kernel
+# launch over its algorithmic bytes, per workload, from captures of the same
+# batches on a 4 GB pool (summaries under profiles/).  bench scales the ratio
+# to the launch it times.
+DECODE_TRAFFIC_RATIO = {"config2": 2.5285 / 2.5180}
+
+
+class DecodeShape:
+    """One decode workload of BASELINE.json: config 2 (Qwen3-0.6B attention,
+    256 seqs/GPU, ctx U[512,4096] or 4096) or config 4 (Llama-3-8B GQA, 32/8
+    heads, 64 seqs/GPU, ctx U[4096,8192])."""
+
+    def __init__(self, args) -> None:
+        self.key = "config4" if args.workload == "llama8b" else "config2"
+        if args.workload == "llama8b":
+            self.name, self.hq, self.batch = "BASELINE config 4: Llama-3-8B GQA long decode", 32, 64
+            self.lo, self.hi, self.default_dtype = 4096, 8192, "bf16"
+            self.ctx_label = "U[4096,8192]"
+        else:
+            self.name, self.hq, self.batch = "BASELINE config 2: paged decode", NUM_Q_HEADS, BATCH_PER_GPU
+            self.lo, self.hi, self.default_dtype = 512, 4096, "fp16"
+            self.ctx_label = "U[512,4096]" if args.ctx == "uniform" else "4096"
+        self.fixed = args.workload != "llama8b" and args.ctx == "fixed4096"
+        self.dtype = args.dtype or self.default_dtype
+
+    def lengths(self, n: int, seed: int) -> list[int]:
+        from micro_vllm_b200.workloads import uniform_lengths
+
+        return [4096] * n if self.fixed else uniform_lengths(n, self.lo, self.hi, seed)
+
+    def bytes(self, ctx: list[int], elsize: int) -> int:
+        return decode_bytes(ctx, elsize, self.hq)
+
+    def label(self) -> str:
+        return (f"{self.name}, {self.batch} seqs/GPU, ctx {self.ctx_label}, Hq {self.hq} / Hkv {NUM_KV_HEADS}, "
+                f"D {HEAD_DIM}, bs {BLOCK_SIZE}")
 
 
 def parse_args() -> argparse.Namespace:
@@ -50,31 +93,24 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--dtype", choices=("fp16", "bf16"), default="fp16")
+    ap.add_argument("--dtype", choices=("fp16", "bf16"), default=None,
+                    help="default: the workload's own (fp16 for config 2, bf16 for configs 3 and 4)")
     ap.add_argument("--ctx", choices=("uniform", "fixed4096"), default="uniform")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--workload", choices=("decode", "mixed"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b"), default="decode",
                     help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
-    ap.add_argument("--mixed-fp16", action="store_true",
-                    help="with --workload mixed and --dtype fp16: run config 3 in fp16")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
     return ap.parse_args()
 
 
-def context_lengths(mode: str, n: int, seed: int) -> list[int]:
-    from micro_vllm_b200.workloads import uniform_lengths
-
-    return [4096] * n if mode == "fixed4096" else uniform_lengths(n, 512, 4096, seed)
-
-
-def decode_bytes(ctx: list[int], elsize: int) -> int:
+def decode_bytes(ctx: list[int], elsize: int, num_q_heads: int = NUM_Q_HEADS) -> int:
     """Algorithmic HBM bytes of one paged decode launch."""
 
     kv = sum(ctx) * NUM_KV_HEADS * HEAD_DIM * 2 * elsize
-    qo = 2 * len(ctx) * NUM_Q_HEADS * HEAD_DIM * elsize
+    qo = 2 * len(ctx) * num_q_heads * HEAD_DIM * elsize
     table = sum(-(-c // BLOCK_SIZE) for c in ctx) * 8
     return kv + qo + table
 
@@ -157,8 +193,9 @@ def cpu_baseline(args, dtype_size: int, seconds: float) -> dict:
     from oracle import build_metadata, paged_attention
 
     cores = os.cpu_count() or 1
-    sample = 32
-    ctx = context_lengths(args.ctx, BATCH_PER_GPU, seed=0)[:sample]
+    shape = DecodeShape(args)
+    sample = min(32, shape.batch)
+    ctx = shape.lengths(shape.batch, seed=0)[:sample]
     rng = np.random.default_rng(0)
     tables, cursor = [], 0
     for c in ctx:
@@ -167,7 +204,7 @@ def cpu_baseline(args, dtype_size: int, seconds: float) -> dict:
         cursor += n
     cache = rng.standard_normal((2, cursor, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
     md = build_metadata([[c - 1] for c in ctx], tables, block_size=BLOCK_SIZE)
-    q = rng.standard_normal((sample, NUM_Q_HEADS, HEAD_DIM), dtype=np.float32)
+    q = rng.standard_normal((sample, shape.hq, HEAD_DIM), dtype=np.float32)
     k = rng.standard_normal((sample, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
     v = rng.standard_normal((sample, NUM_KV_HEADS, HEAD_DIM), dtype=np.float32)
     from threadpoolctl import threadpool_limits
@@ -184,12 +221,12 @@ def cpu_baseline(args, dtype_size: int, seconds: float) -> dict:
                 break
     per_call = elapsed / calls
     return {
-        "value": decode_bytes(ctx, dtype_size) / per_call / 1e9,
+        "value": shape.bytes(ctx, dtype_size) / per_call / 1e9,
         "unit": "GB/s",
         "cores": cores,
         "kind": "port",
         "sample": (
-            f"{sample} of the {BATCH_PER_GPU} decode sequences ({args.ctx} ctx), fp32 numpy port of "
+            f"{sample} of the {shape.batch} decode sequences (ctx {shape.ctx_label}), fp32 numpy port of "
             f"ReferenceAttentionOperator, {calls} calls in {elapsed:.1f}s, "
             f"{per_call * 1e3:.1f} ms/call; bytes counted at {dtype_size}-byte elements like the GPU line"
         ),
@@ -221,8 +258,8 @@ def run_reference(args) -> None:
         "dtype": "f32",
         "data": "synthetic",
         "config": {
-            "workload": f"config2 paged decode, 256 seqs/GPU, ctx {args.ctx}, 16/8 heads, D128, bs16",
-            "sample_sequences": 32,
+            "workload": DecodeShape(args).label(),
+            "sample_sequences": min(32, DecodeShape(args).batch),
         },
         "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -248,14 +285,16 @@ def run_ours(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
+    shape = DecodeShape(args)
+    hq = shape.hq
+    dtype = torch.float16 if shape.dtype == "fp16" else torch.bfloat16
     elsize = 2
 
-    # The global batch (256 sequences per GPU) is split over the ranks by
-    # whole sequences, longest-first to the least-loaded rank.
+    # The global batch (shape.batch sequences per GPU) is split over the ranks
+    # by whole sequences, longest-first to the least-loaded rank.
     from micro_vllm_b200.partition import partition_sequences, sequence_work
 
-    global_ctx = context_lengths(args.ctx, BATCH_PER_GPU * world, seed=1000)
+    global_ctx = shape.lengths(shape.batch * world, seed=1000)
     shards = partition_sequences([sequence_work(c) for c in global_ctx], world)
     ctx = [global_ctx[i] for i in shards[rank].indices]
     local_batch = len(ctx)
@@ -264,13 +303,13 @@ def run_ours(args) -> None:
     else:
         nb = int(args.pool_gb * 1e9) // (2 * BLOCK_SIZE * NUM_KV_HEADS * HEAD_DIM * elsize)
     batch = paged_batch(
-        context_lengths=ctx, query_lengths=[1] * local_batch, num_q_heads=NUM_Q_HEADS,
+        context_lengths=ctx, query_lengths=[1] * local_batch, num_q_heads=hq,
         num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM, block_size=BLOCK_SIZE, num_blocks=nb,
         dtype=dtype, device=dev, seed=2000 + rank,
     )
     op = B200PagedAttentionOperator()
     op.reserve(dev, max_num_tokens=local_batch, max_num_requests=local_batch,
-               num_q_heads=NUM_Q_HEADS, num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM)
+               num_q_heads=hq, num_kv_heads=NUM_KV_HEADS, head_dim=HEAD_DIM)
     stream = torch.cuda.current_stream(dev)
 
     def barrier() -> None:
@@ -289,7 +328,7 @@ def run_ours(args) -> None:
 
     # Attention-only entry point (plan + decode), to time the decode kernel.
     md = batch.metadata
-    ws, st = op._workspace(dev, local_batch, local_batch, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM)
+    ws, st = op._workspace(dev, local_batch, local_batch, hq, NUM_KV_HEADS, HEAD_DIM)
     out_buf = torch.empty_like(batch.query)
     lib = _lib.load()
     attn_args = (
@@ -298,7 +337,7 @@ def run_ours(args) -> None:
         md.query_positions.data_ptr(), md.query_context_start_positions.data_ptr(),
         md.query_start_locations.data_ptr(), md.context_lengths.data_ptr(),
         md.block_table.data_ptr(), md.block_table.stride(0), md.block_table.shape[1],
-        local_batch, local_batch, NUM_Q_HEADS, 1.0 / math.sqrt(HEAD_DIM),
+        local_batch, local_batch, hq, 1.0 / math.sqrt(HEAD_DIM),
         _lib.MVB_DTYPE_F16 if dtype == torch.float16 else _lib.MVB_DTYPE_BF16,
         ws.data_ptr(), ws.numel(), st.status.data_ptr(), stream.cuda_stream,
     )
@@ -369,14 +408,21 @@ def run_ours(args) -> None:
         barrier()
         e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop) / args.steps)
 
-    attn_bytes = decode_bytes(ctx, elsize)  # this rank's share
-    step_bytes_all = decode_bytes(global_ctx, elsize)  # the whole job
+    attn_bytes = shape.bytes(ctx, elsize)  # this rank's share
+    step_bytes_all = shape.bytes(global_ctx, elsize)  # the whole job
     value = step_bytes_all / (step_ms * 1e-3) / 1e9
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peak, peak_src = 6650.0, "fallback"
     if peaks_path.exists():
         peak, peak_src = float(json.loads(peaks_path.read_text())["hbm_gbs"]), "measured"
     achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    ratio = DECODE_TRAFFIC_RATIO.get(shape.key)
+    traffic = None if ratio is None else attn_bytes * ratio
+    traffic_src = (
+        None if ratio is None else
+        f"ncu dram read+write of paged_decode_kernel on this workload's batch (4 GB pool) = {ratio:.4f} x "
+        "algorithmic bytes, scaled to this launch's algorithmic bytes"
+    )
     line = {
         "metric": "paged_decode_hbm_GBps",
         "value": value,
@@ -392,11 +438,10 @@ def run_ours(args) -> None:
         "data": "synthetic",
         "config": {
             "workload": (
-                f"BASELINE config 2: paged decode, {BATCH_PER_GPU} seqs/GPU, ctx "
-                f"{'U[512,4096]' if args.ctx == 'uniform' else '4096'}, Hq 16 / Hkv 8, D 128, bs 16, "
-                f"pool {POOL_FRACTION:.0%} of HBM ({nb} blocks), random block tables; step = KV scatter + decode"
+                f"{shape.label()}, pool {POOL_FRACTION:.0%} of HBM ({nb} blocks), random block tables; "
+                "step = KV scatter + decode"
             ),
-            "global_batch": BATCH_PER_GPU * world,
+            "global_batch": shape.batch * world,
             "parallelism": f"whole-sequence LPT partition over {world} GPU replicas, no data-path collective",
             "l2": "inputs larger than L2 (KV per step about %.2f GB vs 126 MB L2); no flush" % (attn_bytes / 1e9),
             "bytes_per_step_per_gpu": attn_bytes,
@@ -407,7 +452,8 @@ def run_ours(args) -> None:
             "peak": peak,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": None,
+            "traffic": traffic,
+            "traffic_source": traffic_src,
             "peak_source": peak_src,
             "kernel": "paged_decode_kernel (timed with its planner launch, attention-only entry point)",
             "ms_per_launch": attn_ms,
@@ -458,7 +504,7 @@ def run_mixed(args) -> None:
     torch.cuda.set_device(dev)
     # Config 3 is specified in bf16 (the default here); --dtype fp16 runs the
     # same batch in fp16 (the prefill target is quoted against fp16 peak).
-    dtype = torch.float16 if args.dtype == "fp16" and args.mixed_fp16 else torch.bfloat16
+    dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     prefix = uniform_lengths(8, 0, 1024, seed=31)
     new = [2048] * 8
     dec_ctx = uniform_lengths(120, 256, 2048, seed=32)
