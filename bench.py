@@ -53,7 +53,10 @@ POOL_FRACTION = 0.8
 # launch over its algorithmic bytes, per workload, from captures of the same
 # batches on a 4 GB pool (summaries under profiles/).  bench scales the ratio
 # to the launch it times.
-DECODE_TRAFFIC_RATIO = {"config2": 2.5285 / 2.5180}
+# ncu dram read+write bytes of one paged_prefill_kernel launch on the config-3
+# prefill chunks (same seeds, 1 GB pool).
+PREFILL_TRAFFIC = {"bf16": 199.2e6}
+DECODE_TRAFFIC_RATIO = {"config2": 2.5285 / 2.5180, "config4": 1.6174 / 1.6100}
 
 
 class DecodeShape:
@@ -557,6 +560,7 @@ def run_mixed(args) -> None:
     mixed_ms = timed(lambda: op(mixed.query, mixed.key, mixed.value, mixed.cache, mixed.metadata), args.steps)
     clock_info = clocks.stop()
     flops = prefill_flops(prefix, new, NUM_Q_HEADS, HEAD_DIM)
+    dtype_name = "bf16" if dtype == torch.bfloat16 else "fp16"
     achieved = flops / (prefill_ms * 1e-3) / 1e12
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peak, peak_src = 1590.0, "fallback"
@@ -584,7 +588,9 @@ def run_mixed(args) -> None:
             "l2": "prefill re-reads K/V per query tile from L2/HBM; no flush",
         },
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "frac": achieved / peak, "traffic": PREFILL_TRAFFIC.get(dtype_name),
+                     "traffic_source": "ncu dram read+write of paged_prefill_kernel on this batch (1 GB pool)"
+                     if dtype_name in PREFILL_TRAFFIC else None, "peak_source": peak_src,
                      "kernel": "paged_prefill_kernel (with planner; prefill requests only)"},
         "mixed_step": {"ms": mixed_ms, "decode_bytes": dec_bytes,
                        "note": "scatter of 16504 tokens + plan + decode (120 seqs) + prefill (8 chunks)"},
