@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a PTX the prefill kernel uses: mbarriers,
-// per-CTA TMA tile loads, tcgen05 MMA / TMEM access and the shared
+// per-CTA TMA tile loads and stores, tcgen05 MMA / TMEM access and the shared
 // memory matrix descriptors of the 5th-generation tensor cores.
 #pragma once
 
@@ -38,6 +38,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probes of three phases at once: the three tests are in
+// flight together, so their latency (~170 cycles each on sm_100) is paid once.
+__device__ __forceinline__ void mbar_test3(uint32_t b0, uint32_t p0, uint32_t b1, uint32_t p1,
+                                           uint32_t b2, uint32_t p2, bool& r0, bool& r1,
+                                           bool& r2) {
+  uint32_t o0, o1, o2;
+  asm volatile(
+      "{\n\t.reg .pred q0, q1, q2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q0, [%3], %4;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q1, [%5], %6;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q2, [%7], %8;\n\t"
+      "selp.b32 %0, 1, 0, q0;\n\t"
+      "selp.b32 %1, 1, 0, q1;\n\t"
+      "selp.b32 %2, 1, 0, q2;\n\t}"
+      : "=r"(o0), "=r"(o1), "=r"(o2)
+      : "r"(b0), "r"(p0), "r"(b1), "r"(p1), "r"(b2), "r"(p2)
+      : "memory");
+  r0 = o0 != 0;
+  r1 = o1 != 0;
+  r2 = o2 != 0;
+}
 // Bounded wait on the phase with the given parity; false when it never
 // completes (the caller reports the timeout and winds down).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int limit = 1 << 22) {
@@ -62,6 +83,31 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "%3, %4}], [%5];\n" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
+}
+// Tiled TMA store of a 3-D box from shared memory, tracked by this thread's
+// bulk-async group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int32_t x,
+                                             int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(z), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+}
+// This thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
+// This thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
+// Barrier over `count` threads (a multiple of 32) with hardware id `id`.
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 // Generic-proxy writes to shared memory become visible to the async proxy
 // (tensor cores, TMA).
@@ -209,6 +255,32 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+// Packed pairs of fp32 (sm_100 f32x2 instructions: two lanes per op).
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f32x2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // 2^x with the SFU's approximate exp2 (PTX ex2.approx.ftz.f32; -inf -> +0).
