@@ -615,12 +615,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sc[e >> 5][e & 31]),
                                        __uint_as_float(sc[e >> 5][(e & 31) + 1]));
           } else {
+            // Visible keys as one bit per key (window [lo_rel, hi_rel) and
+            // pages present), so each score needs a bit test and a select.
 #pragma unroll
-            for (int e = 0; e < kKeys; ++e) {
-              const bool vis = e >= lo_rel && e < hi_rel && ((pok >> (e >> 4)) & 1u);
-              const float v = vis ? __uint_as_float(sc[e >> 5][e & 31]) : -INFINITY;
-              sc[e >> 5][e & 31] = __float_as_uint(v);
-              mx[e & 3] = fmaxf(mx[e & 3], v);
+            for (int ch = 0; ch < 4; ++ch) {
+              const int a0 = min(max(lo_rel - 32 * ch, 0), 32), b0 = min(max(hi_rel - 32 * ch, 0), 32);
+              const uint32_t below_b = b0 >= 32 ? 0xffffffffu : ((1u << b0) - 1u);
+              const uint32_t below_a = a0 >= 32 ? 0xffffffffu : ((1u << a0) - 1u);
+              const uint32_t pages = (((pok >> (2 * ch)) & 1u) ? 0x0000ffffu : 0u) |
+                                     (((pok >> (2 * ch + 1)) & 1u) ? 0xffff0000u : 0u);
+              const uint32_t vis = below_b & ~below_a & pages;
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float va = (vis >> i) & 1u ? __uint_as_float(sc[ch][i]) : -INFINITY;
+                const float vb = (vis >> (i + 1)) & 1u ? __uint_as_float(sc[ch][i + 1]) : -INFINITY;
+                sc[ch][i] = __float_as_uint(va);
+                sc[ch][i + 1] = __float_as_uint(vb);
+                mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], va, vb);
+              }
             }
           }
           // scale > 0, so the max of the scaled scores is the scaled max.
@@ -686,10 +698,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             f32x2_unpack(ps2[1], s2, s3);
             l += (s0 + s1) + (s2 + s3);
           }
-          if (x == 0) {
+          if (x == 0 && (j == 0 || j == n - 1 || pok != 0xffu)) {
             // Zero V rows no query of the pair may see (below the window,
             // past the last query, or on a missing page): they hold stale or
-            // sentinel bytes that must not reach O as 0 * NaN.
+            // sentinel bytes that must not reach O as 0 * NaN.  Only the
+            // first and last KV tiles hold keys outside [kv_lo, kv_hi].
             const int32_t key = k0 + row;
             const bool zero_row = key < d.kv_lo || key > d.kv_hi || !((pok >> (row >> 4)) & 1u);
             if (zero_row) {
