@@ -35,6 +35,8 @@ WorkspaceLayout workspace_layout(int64_t num_requests, int64_t num_tokens, int32
   off += align256((size_t)(num_requests + 1) * sizeof(int64_t));
   w.prefill_unit_req = off;  // at most one prefill unit per token plus one per request
   off += align256((size_t)(num_tokens + num_requests) * sizeof(int32_t));
+  w.prefill_unit_order = off;  // the same units, most keys first
+  off += align256((size_t)(num_tokens + num_requests) * sizeof(int32_t));
   w.end = off;
   return w;
 }

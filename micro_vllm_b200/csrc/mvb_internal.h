@@ -61,7 +61,7 @@ enum CtrlWord : int {
 // Workspace carve-up.  Offsets depend on (num_requests, num_tokens, num_kv_heads).
 struct WorkspaceLayout {
   size_t ctrl, tile_prefix, cta_start, kind, merge_count, zero_row, partial_ml, partial_o;
-  size_t prefill_prefix, prefill_unit_req, end;
+  size_t prefill_prefix, prefill_unit_req, prefill_unit_order, end;
 };
 
 WorkspaceLayout workspace_layout(int64_t num_requests, int64_t num_tokens, int32_t num_kv_heads);

@@ -6,7 +6,7 @@
 // GQA group; the two tiles (A: the earlier tokens, B: the next ones) share
 // every K/V tile fetched.  A persistent grid (one CTA per SM, 225 KB of
 // shared memory, all 512 TMEM columns) pulls items from an atomic cursor,
-// heaviest (latest) query tiles first.
+// the query tiles with the most keys first.
 //
 // Roles inside a CTA (12 warps), each running its own loop over the items
 // with no block-wide barrier between items, so the next item's loads and
@@ -148,6 +148,7 @@ struct PrefillParams {
   int32_t* cursor;
   const int64_t* unit_prefix;  // per request: first prefill unit (query-tile pair)
   const int32_t* unit_req;     // unit -> request
+  const int32_t* unit_order;   // units, most keys first
   int32_t* status;
 };
 
@@ -292,9 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         d.r = -1;
         d.pad = 0;
         if (claimed < n_items && *abort_flag == 0) {
-          const int64_t it = n_items - 1 - claimed;  // heaviest query tiles first
-          d.h = (int32_t)(it % p.num_kv_heads);
-          const int64_t unit = it / p.num_kv_heads;
+          // Units come longest first (the planner's order), the KV heads of
+          // a unit as consecutive claims.
+          d.h = (int32_t)(claimed % p.num_kv_heads);
+          const int64_t unit = __ldg(p.unit_order + claimed / p.num_kv_heads);
           const int32_t r = __ldg(p.unit_req + unit);
           const int64_t qt = unit - __ldg(p.unit_prefix + r);
           const int64_t qs = __ldg(p.qsl + r), qe = __ldg(p.qsl + r + 1);
@@ -940,6 +942,7 @@ int launch_paged_prefill(const AttentionProblem& a, const WorkspaceLayout& w) {
   pp.cursor = reinterpret_cast<int32_t*>(reinterpret_cast<int64_t*>(ws + w.ctrl) + kCtrlPrefillCursor);
   pp.unit_prefix = reinterpret_cast<const int64_t*>(ws + w.prefill_prefix);
   pp.unit_req = reinterpret_cast<const int32_t*>(ws + w.prefill_unit_req);
+  pp.unit_order = reinterpret_cast<const int32_t*>(ws + w.prefill_unit_order);
   pp.status = a.status;
 
   static int configured_device = -1;

@@ -22,6 +22,7 @@ constexpr int kPlanThreads = 1024;
 struct PlanParams {
   const int64_t* qsl;
   const int64_t* qstart;
+  const int64_t* qpos;
   const int64_t* ctx_len;
   int64_t num_requests;
   int64_t num_tokens;
@@ -42,7 +43,12 @@ struct PlanParams {
   uint4* zero_row;
   int64_t* prefill_prefix;
   int32_t* prefill_unit_req;
+  int32_t* prefill_unit_order;
 };
+
+// Units are ordered by their number of visible keys in 128-key tiles
+// (counting sort, largest first); longer ones share a bucket.
+constexpr int kOrderBuckets = 2048;
 
 // Class and decode tile count of request r.
 __device__ __forceinline__ int64_t request_tiles(const PlanParams& p, int64_t r, int32_t* kind) {
@@ -115,6 +121,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
 
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t total;
+  __shared__ int32_t bucket[kOrderBuckets];
 
   // Per-request decode tile counts and prefill query-tile counts, and their
   // exclusive prefix sums.
@@ -151,6 +158,39 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
   }
   for (int64_t i = threadIdx.x; i < p.num_requests * p.num_kv_heads; i += kPlanThreads)
     p.merge_count[i] = 0;
+
+  // Prefill units, longest first, so the prefill kernel's work cursor hands
+  // out the long query tiles before the short ones and the CTAs finish
+  // together.  Work of a unit ~ the keys its last token sees.
+  if (running_units > 0) {
+    for (int i = threadIdx.x; i < kOrderBuckets; i += kPlanThreads) bucket[i] = 0;
+    __syncthreads();
+    auto unit_bucket = [&](int64_t u) -> int32_t {
+      const int64_t r = p.prefill_unit_req[u];
+      const int64_t qs = p.qsl[r], qe = p.qsl[r + 1];
+      const int64_t first = qs + (u - p.prefill_prefix[r]) * p.prefill_block_q;
+      const int64_t last = min(first + p.prefill_block_q, qe) - 1;
+      const int64_t lo = max(max(p.qstart[qs], (int64_t)0), min(p.qstart[first], p.qstart[last]));
+      const int64_t hi = min(p.ctx_len[r] - 1, p.qpos[last]);
+      const int64_t tiles = hi >= lo ? ((hi - lo) >> 7) + 1 : 0;
+      return (int32_t)(kOrderBuckets - 1 - min(tiles, (int64_t)kOrderBuckets - 1));  // descending
+    };
+    for (int64_t u = threadIdx.x; u < running_units; u += kPlanThreads)
+      atomicAdd(&bucket[unit_bucket(u)], 1);
+    __syncthreads();
+    // Exclusive scan of the bucket counts (2 per thread).
+    {
+      const int i0 = 2 * threadIdx.x;
+      const int64_t c0 = bucket[i0], c1 = bucket[i0 + 1];
+      const int64_t incl = block_inclusive_scan(c0 + c1, warp_tot, &total);
+      __syncthreads();
+      bucket[i0] = (int32_t)(incl - c0 - c1);
+      bucket[i0 + 1] = (int32_t)(incl - c1);
+    }
+    __syncthreads();
+    for (int64_t u = threadIdx.x; u < running_units; u += kPlanThreads)
+      p.prefill_unit_order[atomicAdd(&bucket[unit_bucket(u)], 1)] = (int32_t)u;
+  }
   if (threadIdx.x < kMaxHeadsPerCta * 256 / 16) p.zero_row[threadIdx.x] = make_uint4(0, 0, 0, 0);
   __syncthreads();  // tile_prefix complete before the searches below
 
@@ -184,6 +224,7 @@ int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t gro
   PlanParams p;
   p.qsl = a.qsl;
   p.qstart = a.qstart;
+  p.qpos = a.qpos;
   p.ctx_len = a.ctx_len;
   p.num_requests = a.num_requests;
   p.num_tokens = a.num_tokens;
@@ -204,6 +245,7 @@ int launch_plan(const AttentionProblem& a, const WorkspaceLayout& w, int32_t gro
   p.zero_row = reinterpret_cast<uint4*>(ws + w.zero_row);
   p.prefill_prefix = reinterpret_cast<int64_t*>(ws + w.prefill_prefix);
   p.prefill_unit_req = reinterpret_cast<int32_t*>(ws + w.prefill_unit_req);
+  p.prefill_unit_order = reinterpret_cast<int32_t*>(ws + w.prefill_unit_order);
   // Block 0 plans; 32 more blocks zero padding rows (enough for a few MB).
   plan_kernel<<<33, kPlanThreads, 0, a.stream>>>(p);
   return check_launch();
