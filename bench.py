@@ -55,7 +55,7 @@ POOL_FRACTION = 0.8
 # to the launch it times.
 # ncu dram read+write bytes of one paged_prefill_kernel launch on the config-3
 # prefill chunks (same seeds, 1 GB pool).
-PREFILL_TRAFFIC = {"bf16": 199.2e6}
+PREFILL_TRAFFIC = {"fp16": 396.8e6}
 DECODE_TRAFFIC_RATIO = {"config2": 2.5285 / 2.5180, "config4": 1.6174 / 1.6100}
 
 
