@@ -13,16 +13,19 @@
 // first MMAs overlap the current item's last tiles and epilogue:
 //   warp 11  scheduler: claims the next item, computes its description
 //           (request, tokens, KV head, the union of its rows' key windows
-//           and so the KV tiles to visit) and publishes it in a 2-slot ring.
-//   warps 8, 10  TMA producers (Q and K, and V): both Q tiles once per item
-//           (a 3-D tensor map over [token, head, dim] so the G heads of a
-//           token land in adjacent rows), into a Q buffer freed by the
-//           item's last S MMA; per 128-key KV tile, the 8 pages of K and V
+//           and so the KV tiles to visit), publishes it in a 2-slot ring and
+//           loads the item's Q tiles (a 3-D tensor map over [token, head,
+//           dim] so the G heads of a token land in adjacent rows), each into
+//           its tile's buffer once the previous item's epilogue released it.
+//   warps 8, 10  TMA producers of K and V: per 128-key KV tile, the 8 pages
 //           (a 2-D tensor map over the cache's [2*NB*bs slots, Hkv*128]
 //           view; one 16-row x 64-element box per page, plane and half)
 //           into a 2-stage K ring and a 3-stage V ring, 128-byte swizzled —
 //           the layout the tensor cores read.  Pages missing from the block
-//           table are fetched from page 0 and masked.
+//           table are fetched from page 0 and masked.  Warp 10 then zeroes
+//           the rows of each landed V tile that no query of the pair may see
+//           (stale or sentinel bytes must not reach O as 0 * NaN) before the
+//           P.V MMAs may read it.
 //   warp 9  MMA issuer (one thread), ping-pong between the tiles:
 //             S_A(0), S_B(0); then per KV tile j:
 //             PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
@@ -40,11 +43,11 @@
 //           PV_X(j-1), complete since S_X(j) is); pass 2 computes
 //           P = 2^(s - max) from the same registers and stores it to TMEM.
 //           bf16 P is split into P_hi + P_lo (two MMAs) to keep ~16 bits.
-//           Tile A's warps also zero V rows no query of the pair may see, so
-//           stale cache bytes cannot reach O as 0 * NaN.  At the end each
-//           row's O is normalised and stored; the next item's first P.V
-//           (which overwrites O_X) waits for this warp's next P, so it
-//           cannot start before these loads.
+//           At the end
+//           each row's O is normalised and staged in the tile's Q buffer
+//           (every S of the item is done with it) for two TMA stores; the
+//           next item's first P.V (which overwrites O_X) waits for this
+//           warp's next P, so it cannot start before these loads.
 // The softmax warpgroups (warps 0-7) raise their register limit to 200 and
 // the other warpgroup (warps 8-11) lowers its own to 96, which fits in the
 // 168 per thread the block is launched with (the host checks that count).
@@ -103,7 +106,8 @@ enum Bar : int {
   kKEmpty = kKFull + kKStages,          // +K slot: every S MMA read it
   kVFull = kKEmpty + kKStages,          // +V slot: V tile landed
   kVEmpty = kVFull + kVStages,          // +V slot: every P.V MMA read it
-  kSFull = kVEmpty + kVStages,          // +tile (A, B)
+  kVReady = kVEmpty + kVStages,         // +V slot: the V producer fixed the tile up
+  kSFull = kVReady + kVStages,          // +tile (A, B)
   kPFull = kSFull + 2,                  // +tile
   kPvDone = kPFull + 2,                 // +tile
   kOStaged = kPvDone + 2,               // +tile: the 4 warps staged O for the TMA store
@@ -112,7 +116,7 @@ enum Bar : int {
   kFinal = kItemEmpty + kItemSlots,     // last MMA commit before TMEM is released
   kNumBars = kFinal + 1,
 };
-static_assert(kNumBars == 4 + 2 * kKStages + 2 * kVStages + 4 * 2 + 2 * kItemSlots + 1,
+static_assert(kNumBars == 4 + 2 * kKStages + 3 * kVStages + 4 * 2 + 2 * kItemSlots + 1,
               "mbarrier layout");
 
 // One work item as the scheduler warp describes it.
@@ -216,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kVStages; ++s) {
       mbar_init(bar(kVFull + s), 1);
       mbar_init(bar(kVEmpty + s), 1);
+      mbar_init(bar(kVReady + s), 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(kSFull + s), 1);
@@ -387,12 +392,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto issue_pv = [&](int t, uint32_t stage, bool acc) {
           const uint64_t dv = dv0 + (uint64_t)((stage * kTileBytes) >> 4);
           const uint32_t d_tmem = tmem + col_o(t), p_tmem = tmem + col_s(t);
+          const uint32_t idesc = idesc_pv;
 #pragma unroll
           for (int part = 0; part < (kBf16 ? 2 : 1); ++part) {  // P_hi (+ P_lo in bf16)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t pcol = 32 * (k >> 1) + 8 * (k & 1) + 16 * part;
-              umma_f16_ts(d_tmem, p_tmem + pcol, dv + (uint64_t)(k * (2048 >> 4)), idesc_pv,
+              umma_f16_ts(d_tmem, p_tmem + pcol, dv + (uint64_t)(k * (2048 >> 4)), idesc,
                           acc || k > 0 || part > 0);
             }
           }
@@ -452,11 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (t == 0) {
                 // P_A(j), V(j) and K(j+1) probed together.
                 bool rp, rv, rk;
-                mbar_test3(bar(kPFull), pphase, bar(kVFull + sv), vphase(c),
+                mbar_test3(bar(kPFull), pphase, bar(kVReady + sv), vphase(c),
                            more ? bar(kKFull + skn) : bar(kPFull), more ? kphase(cn) : pphase, rp,
                            rv, rk);
                 ok = (rp || mbar_wait(bar(kPFull), pphase)) &&
-                     (rv || mbar_wait(bar(kVFull + sv), vphase(c)));
+                     (rv || mbar_wait(bar(kVReady + sv), vphase(c)));
                 k_ready = rk;
               } else {
                 ok = mbar_wait(bar(kPFull + t), pphase);
@@ -527,6 +533,42 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t dst = sb + (is_k ? kOffK : kOffV) + slot_kv * kTileBytes + lane * 2048;
               tma_load_2d(dst, &kvmap, xk, y, full);
               tma_load_2d(dst + kHalf, &kvmap, xk + 64, y, full);
+            }
+            if (!is_k) {
+              // V(c) landed: zero the rows no query of the pair may see (they
+              // hold stale or sentinel bytes that must not reach O as 0 * NaN;
+              // only the first and last tile and missing pages have any), then
+              // release the tile to the P.V MMAs.  Lane l walks rows 4i + l/8
+              // at 16-byte chunk l%8: conflict-free.
+              const uint32_t pok = __ballot_sync(0xffffffffu, lane < 8 && blk >= 0) & 0xffu;
+              if (j == 0 || j == n - 1 || pok != 0xffu) {
+                if (!__all_sync(0xffffffffu, mbar_wait(full, vphase(c)))) {
+                  ok = false;
+                  break;
+                }
+                uint8_t* vt = smem + kOffV + slot_kv * kTileBytes;
+                const int32_t k0 = d.kbase + j * kKeys;
+#pragma unroll 4
+                for (int it = 0; it < 32; ++it) {
+                  const int row = 4 * it + (lane >> 3), cc = lane & 7;
+                  const int32_t key = k0 + row;
+                  if (key < d.kv_lo || key > d.kv_hi || !((pok >> (row >> 4)) & 1u)) {
+                    *reinterpret_cast<uint4*>(vt + row * 128 + cc * 16) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(vt + kHalf + row * 128 + cc * 16) = make_uint4(0, 0, 0, 0);
+                  }
+                }
+                fence_proxy_async();  // visible to the P.V MMAs
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kVReady + slot_kv));
+              } else if (lane == 0) {
+                // Nothing to fix: the tile is ready once it lands.
+                if (!mbar_wait(full, vphase(c))) ok = false;
+                mbar_arrive(bar(kVReady + slot_kv));
+              }
+              if (!__all_sync(0xffffffffu, ok)) {
+                ok = false;
+                break;
+              }
             }
           }
           ok = __all_sync(0xffffffffu, ok);
@@ -667,30 +709,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t scale2 = f32x2_pack(p.scale_log2, p.scale_log2);
           const uint64_t negmu2 = f32x2_pack(-mu, -mu);
           uint64_t ps2[2] = {f32x2_pack(0.f, 0.f), f32x2_pack(0.f, 0.f)};
+          // P as packed 16-bit pairs; bf16 P as P_hi + P_lo (columns
+          // 32ch..+15 and 32ch+16..+31).
+          {
+            constexpr bool kSplit = kBf16;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {  // 16 keys: 8 packed columns per store
-              uint32_t hi[8], lo[8];
+              for (int hh = 0; hh < 2; ++hh) {  // 16 keys: 8 packed columns per store
+                uint32_t hi[8], lo[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int k = 16 * hh + 2 * e;
-                float xa, xb;
-                f32x2_unpack(f32x2_fma(f32x2_pack(__uint_as_float(sc[ch][k]),
-                                                  __uint_as_float(sc[ch][k + 1])),
-                                       scale2, negmu2),
-                             xa, xb);
-                const float pa = ex2(xa), pb = ex2(xb);
-                ps2[e & 1] = f32x2_add(ps2[e & 1], f32x2_pack(pa, pb));
-                hi[e] = pack2<T>(pa, pb);
-                if constexpr (kBf16) {
-                  const float2 hf =
-                      __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi[e]));
-                  lo[e] = pack2<T>(pa - hf.x, pb - hf.y);
+                for (int e = 0; e < 8; ++e) {
+                  const int k = 16 * hh + 2 * e;
+                  float xa, xb;
+                  f32x2_unpack(f32x2_fma(f32x2_pack(__uint_as_float(sc[ch][k]),
+                                                    __uint_as_float(sc[ch][k + 1])),
+                                         scale2, negmu2),
+                               xa, xb);
+                  const float pa = ex2(xa), pb = ex2(xb);
+                  ps2[e & 1] = f32x2_add(ps2[e & 1], f32x2_pack(pa, pb));
+                  hi[e] = pack2<T>(pa, pb);
+                  if constexpr (kSplit) {
+                    const float2 hf =
+                        __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi[e]));
+                    lo[e] = pack2<T>(pa - hf.x, pb - hf.y);
+                  }
                 }
+                tmem_st8(s_cols + 32 * ch + 8 * hh, hi);
+                if constexpr (kSplit) tmem_st8(s_cols + 32 * ch + 16 + 8 * hh, lo);
               }
-              tmem_st8(s_cols + 32 * ch + 8 * hh, hi);
-              if constexpr (kBf16) tmem_st8(s_cols + 32 * ch + 16 + 8 * hh, lo);
             }
           }
           tmem_wait_st();
@@ -699,26 +746,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             f32x2_unpack(ps2[0], s0, s1);
             f32x2_unpack(ps2[1], s2, s3);
             l += (s0 + s1) + (s2 + s3);
-          }
-          if (x == 0 && (j == 0 || j == n - 1 || pok != 0xffu)) {
-            // Zero V rows no query of the pair may see (below the window,
-            // past the last query, or on a missing page): they hold stale or
-            // sentinel bytes that must not reach O as 0 * NaN.  Only the
-            // first and last KV tiles hold keys outside [kv_lo, kv_hi].
-            const int32_t key = k0 + row;
-            const bool zero_row = key < d.kv_lo || key > d.kv_hi || !((pok >> (row >> 4)) & 1u);
-            if (zero_row) {
-              // V(j) must have landed before its rows are overwritten.
-              if (!mbar_wait(bar(kVFull + sv), vphase(c))) ok = false;
-              uint8_t* vrow = smem + kOffV + sv * kTileBytes + row * 128;
-              const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-              for (int cc = 0; cc < 8; ++cc) {
-                *reinterpret_cast<uint4*>(vrow + cc * 16) = z;
-                *reinterpret_cast<uint4*>(vrow + kHalf + cc * 16) = z;
-              }
-              fence_proxy_async();  // the zeros are visible to the P.V MMA
-            }
           }
           tc_fence_before();
           __syncwarp();

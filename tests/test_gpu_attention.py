@@ -344,6 +344,28 @@ def test_prefill_sliding_window_on_tensor_cores(window: int) -> None:
     _run_and_check(batch)
 
 
+def test_prefill_bf16_values_beyond_fp16_range() -> None:
+    """bf16 V tiles are converted to fp16 for the P.V MMA only when every
+    visible value fits fp16; tiles holding |v| > 65504 (and one with
+    subnormal-range values) must give the same answer on the exact path."""
+
+    ctx = [1000, 700, 900]
+    qlen = [400, 700, 300]
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=400, dtype=torch.bfloat16, device=DEV, seed=77,
+    )
+    table = batch.metadata.block_table.cpu()
+    # Request 0: cached prefix keys with values past the fp16 maximum in two
+    # different 128-key tiles, and tiny ones in a third.
+    for pos, val in ((5, 7.0e4), (300, -1.0e5), (450, 3.0e-6)):
+        page, off = int(table[0, pos // 16]), pos % 16
+        batch.cache[1, page, off, 2] = val
+    # Request 1 (fresh prompt): one written value past the fp16 maximum.
+    batch.value[400 + 123, 5] = 9.0e4
+    _run_and_check(batch)
+
+
 def test_prefill_repeated_calls_reuse_the_workspace() -> None:
     """Several different mixed batches through one operator instance (the
     persistent kernels' barrier phases and work cursors restart cleanly)."""
