@@ -446,38 +446,70 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     for (int64_t b = b_first; b <= b_last; ++b)
       nseg += (b * n_all / grid) < ((b + 1) * n_all / grid);
     if (done != nseg - 1) continue;
-    // Last segment to finish: merge all segments of (request, kvh).
+    // Last segment to finish: merge all segments of (request, kvh).  The
+    // segments' (max, sum) pairs are loaded one per lane and combined with
+    // shuffles; the partial O rows are then read several at a time, so the
+    // merge costs a few L2 round trips rather than two per segment.
     __threadfence();
+    // Partial slot of CTA b for this request: 0 when it is the first request
+    // of b's share, else 1.
+    auto partial_index = [&](int64_t b) -> int64_t {
+      const int64_t bstart = b * n_all / grid;
+      const int64_t bfirst_vr = (bstart / tiles) * p.num_requests + __ldg(p.cta_start + b);
+      return (b * 2 + (bfirst_vr == cur_vr ? 0 : 1)) * kMaxHeadsPerCta + w;
+    };
+    auto non_empty = [&](int64_t b) { return (b * n_all / grid) < ((b + 1) * n_all / grid); };
+    const int64_t nb = b_last - b_first + 1;
     for (int n = 0; n < ncols; ++n) {
+      // Pass 1: the reference max over the segments.
       float mx = -INFINITY;
-      for (int64_t b = b_first; b <= b_last; ++b) {
-        const int64_t bstart = b * n_all / grid;
-        if (bstart == (b + 1) * n_all / grid) continue;  // empty share
-        const int64_t bfirst_vr = (bstart / tiles) * p.num_requests + __ldg(p.cta_start + b);
-        const int sl = (bfirst_vr == cur_vr) ? 0 : 1;
-        const int64_t idx = (b * 2 + sl) * kMaxHeadsPerCta + w;
-        mx = fmaxf(mx, __ldcg(&p.partial_ml[idx * kDecodeCols + n].x));
+      for (int64_t b0 = b_first; b0 <= b_last; b0 += 32) {
+        const int64_t b = b0 + lane;
+        if (b <= b_last && non_empty(b))
+          mx = fmaxf(mx, __ldcg(&p.partial_ml[partial_index(b) * kDecodeCols + n].x));
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float mu = mx == -INFINITY ? 0.f : mx;
+      // Pass 2: weighted sums; lane k of each group of 32 segments holds
+      // segment k's weight and partial index.
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       float sum = 0.f;
-      for (int64_t b = b_first; b <= b_last; ++b) {
-        const int64_t bstart = b * n_all / grid;
-        if (bstart == (b + 1) * n_all / grid) continue;  // empty share
-        const int64_t bfirst_vr = (bstart / tiles) * p.num_requests + __ldg(p.cta_start + b);
-        const int sl = (bfirst_vr == cur_vr) ? 0 : 1;
-        const int64_t idx = (b * 2 + sl) * kMaxHeadsPerCta + w;
-        const float2 ml = __ldcg(&p.partial_ml[idx * kDecodeCols + n]);
-        const float f = exp2f(ml.x - mu);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                                    p.partial_o + (idx * kDecodeCols + n) * kDecodeHeadDim) +
-                                lane);
-        acc.x += v.x * f;
-        acc.y += v.y * f;
-        acc.z += v.z * f;
-        acc.w += v.w * f;
-        sum += ml.y * f;
+      for (int64_t b0 = b_first; b0 <= b_last; b0 += 32) {
+        const int64_t b = b0 + lane;
+        float f = 0.f;
+        int64_t idx = 0;
+        if (b <= b_last && non_empty(b)) {
+          idx = partial_index(b);
+          const float2 ml = __ldcg(&p.partial_ml[idx * kDecodeCols + n]);
+          f = exp2f(ml.x - mu);
+          sum += ml.y * f;
+        }
+        const int cnt = (int)min((int64_t)32, nb - (b0 - b_first));
+        for (int k0 = 0; k0 < cnt; k0 += 4) {
+          float4 v[4];
+          float fk[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k = min(k0 + u, cnt - 1);
+            fk[u] = k0 + u < cnt ? __shfl_sync(0xffffffffu, f, k) : 0.f;
+            const int64_t ik = __shfl_sync(0xffffffffu, idx, k);
+            v[u] = fk[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(
+                                          p.partial_o + (ik * kDecodeCols + n) * kDecodeHeadDim) +
+                                      lane)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc.x += v[u].x * fk[u];
+            acc.y += v[u].y * fk[u];
+            acc.z += v[u].z * fk[u];
+            acc.w += v[u].w * fk[u];
+          }
+        }
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       const float inv = sum > 0.f ? 1.f / sum : NAN;
       const int64_t t = e.qs + n / p.group;
       const int hq = kvh * p.group + n % p.group;
