@@ -460,6 +460,53 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     };
     auto non_empty = [&](int64_t b) { return (b * n_all / grid) < ((b + 1) * n_all / grid); };
     const int64_t nb = b_last - b_first + 1;
+    if (nb * ncols <= 32) {
+      // Common case: every (segment, column) pair fits one lane, so all the
+      // (max, sum) pairs and then all the partial rows are loaded at once.
+      const int nbi = (int)nb;
+      const int s_l = lane % nbi, n_l = lane / nbi;  // this lane's pair
+      const int64_t b_l = b_first + s_l;
+      const bool live = n_l < ncols && non_empty(b_l);
+      const int64_t idx_l = live ? partial_index(b_l) : 0;
+      float2 ml = make_float2(-INFINITY, 0.f);
+      if (live) ml = __ldcg(&p.partial_ml[idx_l * kDecodeCols + n_l]);
+      float mx_l = -INFINITY;  // max over this lane's column
+      for (int k = 0; k < nbi; ++k)
+        mx_l = fmaxf(mx_l, __shfl_sync(0xffffffffu, ml.x, min(n_l, ncols - 1) * nbi + k));
+      const float f_l = live ? exp2f(ml.x - (mx_l == -INFINITY ? 0.f : mx_l)) : 0.f;
+      float sum_l = 0.f;  // sum over this lane's column
+      for (int k = 0; k < nbi; ++k) {
+        const int src = min(n_l, ncols - 1) * nbi + k;
+        sum_l += __shfl_sync(0xffffffffu, ml.y * f_l, src);
+      }
+      for (int n = 0; n < ncols; ++n) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int k = 0; k < nbi; ++k) {
+          const int src = n * nbi + k;
+          const float fk = __shfl_sync(0xffffffffu, f_l, src);
+          const int64_t ik = __shfl_sync(0xffffffffu, idx_l, src);
+          const float4 v = fk != 0.f ? __ldcg(reinterpret_cast<const float4*>(
+                                               p.partial_o + (ik * kDecodeCols + n) * kDecodeHeadDim) +
+                                           lane)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+          acc.x += v.x * fk;
+          acc.y += v.y * fk;
+          acc.z += v.z * fk;
+          acc.w += v.w * fk;
+        }
+        const float sum = __shfl_sync(0xffffffffu, sum_l, n * nbi);
+        const float inv = sum > 0.f ? 1.f / sum : NAN;
+        const int64_t t = e.qs + n / p.group;
+        const int hq = kvh * p.group + n % p.group;
+        T* orow = reinterpret_cast<T*>(p.out) + (t * p.num_q_heads + hq) * kDecodeHeadDim + 4 * lane;
+        orow[0] = from_float<T>(empty_history ? 0.f : acc.x * inv);
+        orow[1] = from_float<T>(empty_history ? 0.f : acc.y * inv);
+        orow[2] = from_float<T>(empty_history ? 0.f : acc.z * inv);
+        orow[3] = from_float<T>(empty_history ? 0.f : acc.w * inv);
+      }
+      continue;
+    }
     for (int n = 0; n < ncols; ++n) {
       // Pass 1: the reference max over the segments.
       float mx = -INFINITY;
