@@ -172,6 +172,39 @@ MVB_API int mvb_paged_attention_no_alloc(const void* query, int64_t query_token_
                                          int64_t num_requests, int32_t num_q_heads, float scale,
                                          int32_t dtype, int32_t* status, void* stream);
 
+/*
+ * Fused Qwen3 attention prologue: per-head RMSNorm of query and key, rotary
+ * position embedding of both, and the KV-cache write — one launch.
+ *
+ * Replaces, in one call, what Qwen3Attention.forward does between the
+ * projections and the attention operator (src/micro_vllm/models/qwen.py:89-91):
+ * q_norm / k_norm (RMSNorm.forward, src/micro_vllm/layers/normalization.py:15-22),
+ * RotaryEmbedding.forward (src/micro_vllm/layers/rotary_embedding.py:22-52),
+ * and the operator's first step write_kv_cache
+ * (src/micro_vllm/attention/operators/reference.py:84-98).
+ *
+ * query [T, Hq, 128], key / value [T, Hkv, 128]: element strides
+ * q/k/v_strides[3] (host arrays), unit innermost stride, rows 8-byte
+ * aligned.  q_out [T, Hq, 128] contiguous receives the normalised, rotated
+ * query; kv_cache plane 0 receives the normalised, rotated key and plane 1
+ * the value at slot_mapping[t] (negative slot: nothing; past the pool:
+ * nothing and MVB_STATUS_SLOT_OUT_OF_RANGE).  q_weight / k_weight [128] are
+ * the RMSNorm weights in the activation dtype; inv_freq [64] (fp32) the
+ * rotary inverse frequencies 1 / base^(2i/128) evaluated by the caller as the
+ * reference does; positions [T] int64.  dtype MVB_DTYPE_F16 or _BF16.
+ * head_dim must be 128 (else MVB_ERR_UNSUPPORTED_SHAPE).
+ */
+MVB_API int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strides,
+                                       const void* key, const int64_t* k_strides,
+                                       const void* value, const int64_t* v_strides, void* q_out,
+                                       const void* q_weight, const void* k_weight, float eps,
+                                       const float* inv_freq, const int64_t* positions,
+                                       void* kv_cache, int64_t num_blocks, int32_t block_size,
+                                       int32_t num_kv_heads, int32_t head_dim,
+                                       const int64_t* slot_mapping, int64_t num_tokens,
+                                       int32_t num_q_heads, int32_t dtype, int32_t* status,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

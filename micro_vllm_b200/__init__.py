@@ -1,7 +1,8 @@
 """B200 (sm_100a) paged-attention backend for micro-vLLM.
 
 The hot path of micro-vLLM's attention-operator layer — the KV-cache scatter
-and paged attention over that cache — as hand-written CUDA behind a C ABI
+and paged attention over that cache, plus the fused q/k-norm + RoPE + KV-write
+prologue of a Qwen3 layer — as hand-written CUDA behind a C ABI
 (include/mvb200.h, ``libmvb200.so``), with a Python operator that mirrors
 the reference's ``AttentionOperator`` interface.
 """
@@ -22,6 +23,11 @@ from micro_vllm_b200.operators import (  # noqa: F401
     get_attention_operator_class,
     write_kv_cache,
 )
+from micro_vllm_b200.prologue import (  # noqa: F401
+    Qwen3AttentionPrologue,
+    qk_norm_rope_and_write,
+    rotary_inverse_frequencies,
+)
 
 __all__ = [
     "Attention",
@@ -32,8 +38,11 @@ __all__ = [
     "ChunkedLocalSpec",
     "FullAttentionSpec",
     "OPERATOR_NAME",
+    "Qwen3AttentionPrologue",
     "SlidingWindowSpec",
     "get_attention_operator_class",
     "map_cache_slots",
+    "qk_norm_rope_and_write",
+    "rotary_inverse_frequencies",
     "write_kv_cache",
 ]

@@ -63,6 +63,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _P, _P,  # status, stream
         ],
     ),
+    "mvb_qk_norm_rope_and_cache": (
+        ctypes.c_int,
+        [
+            _P, _P, _P, _P, _P, _P,  # query, strides, key, strides, value, strides
+            _P, _P, _P, _F32, _P, _P,  # q_out, q_weight, k_weight, eps, inv_freq, positions
+            _P, _I64, _I32, _I32, _I32,  # cache, NB, bs, Hkv, D
+            _P, _I64, _I32, _I32, _P, _P,  # slots, T, Hq, dtype, status, stream
+        ],
+    ),
     "mvb_attention_forward": (
         ctypes.c_int,
         [

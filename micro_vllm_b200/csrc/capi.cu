@@ -161,4 +161,47 @@ int mvb_attention_forward(const void* query, int64_t query_token_stride, int64_t
                              status, stream);
 }
 
+int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strides, const void* key,
+                               const int64_t* k_strides, const void* value,
+                               const int64_t* v_strides, void* q_out, const void* q_weight,
+                               const void* k_weight, float eps, const float* inv_freq,
+                               const int64_t* positions, void* kv_cache, int64_t num_blocks,
+                               int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                               const int64_t* slot_mapping, int64_t num_tokens,
+                               int32_t num_q_heads, int32_t dtype, int32_t* status, void* stream) {
+  if (dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens < 0 || num_blocks < 0 || block_size <= 0 || num_kv_heads <= 0 ||
+      num_q_heads <= 0 || head_dim <= 0 || !(eps >= 0.f))
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MVB_OK;
+  if (!query || !key || !value || !q_out || !q_weight || !k_weight || !inv_freq || !positions ||
+      !kv_cache || !slot_mapping || !q_strides || !k_strides || !v_strides)
+    return MVB_ERR_INVALID_ARGUMENT;
+  QkPrologueArgs a;
+  a.query = query;
+  a.q_strides = q_strides;
+  a.key = key;
+  a.k_strides = k_strides;
+  a.value = value;
+  a.v_strides = v_strides;
+  a.q_out = q_out;
+  a.q_weight = q_weight;
+  a.k_weight = k_weight;
+  a.eps = eps;
+  a.inv_freq = inv_freq;
+  a.positions = positions;
+  a.kv_cache = kv_cache;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.num_kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.slot_mapping = slot_mapping;
+  a.num_tokens = num_tokens;
+  a.num_q_heads = num_q_heads;
+  a.dtype = dtype;
+  a.status = status;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_qk_prologue(a);
+}
+
 }  // extern "C"

@@ -94,6 +94,30 @@ bool prefill_tc_supported(const AttentionProblem& p);
 int prefill_tokens_per_unit(int32_t group);
 int launch_paged_prefill(const AttentionProblem& p, const WorkspaceLayout& w);
 
+struct QkPrologueArgs {
+  const void* query;
+  const int64_t* q_strides;
+  const void* key;
+  const int64_t* k_strides;
+  const void* value;
+  const int64_t* v_strides;
+  void* q_out;
+  const void* q_weight;
+  const void* k_weight;
+  float eps;
+  const float* inv_freq;
+  const int64_t* positions;
+  void* kv_cache;
+  int64_t num_blocks;
+  int32_t block_size, num_kv_heads, head_dim;
+  const int64_t* slot_mapping;
+  int64_t num_tokens;
+  int32_t num_q_heads, dtype;
+  int32_t* status;
+  cudaStream_t stream;
+};
+int launch_qk_prologue(const QkPrologueArgs& a);
+
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,
                 int32_t decode_ctas, int32_t prefill_block_q);
 int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w, int32_t grid,

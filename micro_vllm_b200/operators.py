@@ -178,6 +178,54 @@ class B200PagedAttentionOperator(AttentionOperator):
         return output
 
 
+    # -- attention over a cache that already holds this step's keys/values
+    def attend(self, query, layer_kv_cache, metadata) -> torch.Tensor:
+        """Paged attention of ``query`` over ``layer_kv_cache`` without the KV
+        write (reference.py:26-81 after its write_kv_cache line): for callers
+        whose prologue (``qk_norm_rope_and_write``) wrote the keys and values."""
+
+        for t in (query, layer_kv_cache):
+            if t.device.type != "cuda":
+                raise RuntimeError("b200_paged attention requires CUDA tensors")
+        dtype = _DTYPES.get(query.dtype)
+        if dtype is None or layer_kv_cache.dtype != query.dtype:
+            raise ValueError("query and layer_kv_cache must share a float16/bfloat16/float32 dtype")
+        if query.dim() != 3 or layer_kv_cache.dim() != 5 or not layer_kv_cache.is_contiguous():
+            raise ValueError("expected query [T,H,D] and a contiguous layer_kv_cache [2,NB,bs,Hkv,D]")
+        num_tokens, num_q_heads, head_dim = query.shape
+        _, num_blocks, block_size, num_kv_heads, cache_dim = layer_kv_cache.shape
+        if cache_dim != head_dim or block_size != metadata.block_size:
+            raise ValueError("layer_kv_cache does not match the query / metadata")
+        if num_q_heads % num_kv_heads != 0:
+            raise ValueError("num_q_heads must be a multiple of num_kv_heads")
+        device = query.device
+        if query.stride(2) != 1:
+            query = query.contiguous()
+        md_pos = _meta(metadata.query_positions, device, "query_positions")
+        md_start = _meta(metadata.query_context_start_positions, device, "query_context_start_positions")
+        md_qsl = _meta(metadata.query_start_locations, device, "query_start_locations")
+        md_ctx = _meta(metadata.context_lengths, device, "context_lengths")
+        table = metadata.block_table
+        if table.dtype != torch.int64 or table.device != device:
+            raise ValueError("metadata.block_table must be torch.int64 on the query's device")
+        if table.dim() != 2 or (table.shape[1] > 1 and table.stride(1) != 1):
+            table = table.reshape(md_ctx.numel(), -1).contiguous()
+        num_requests = md_ctx.numel()
+        output = torch.empty((num_tokens, num_q_heads, head_dim), dtype=query.dtype, device=device)
+        workspace, st = self._workspace(device, num_tokens, num_requests, num_q_heads, num_kv_heads, head_dim)
+        rc = self._lib.mvb_paged_attention(
+            query.data_ptr(), query.stride(0), query.stride(1), output.data_ptr(),
+            layer_kv_cache.data_ptr(), num_blocks, block_size, num_kv_heads, head_dim,
+            md_pos.data_ptr(), md_start.data_ptr(), md_qsl.data_ptr(), md_ctx.data_ptr(),
+            table.data_ptr(), table.stride(0) if table.shape[1] > 0 else 0, table.shape[1],
+            num_tokens, num_requests, num_q_heads, 1.0 / math.sqrt(head_dim), dtype,
+            workspace.data_ptr(), workspace.numel(), st.status.data_ptr(),
+            torch.cuda.current_stream(device).cuda_stream,
+        )
+        _lib.check(rc, "b200_paged attention")
+        return output
+
+
 def write_kv_cache(key, value, layer_kv_cache, metadata) -> None:
     """The KV scatter alone (reference.py:84-98), for ModelRunner-side writes."""
 

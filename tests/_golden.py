@@ -50,3 +50,40 @@ def oracle_metadata(case: dict):
         slot_mapping=case["slot_mapping"],
         block_size=case["block_size"],
     )
+
+
+# ---------------------------------------------------------------- prologue
+PROLOGUE_CASES = ("qwen3_f16", "qwen3_bf16", "gqa4_long_f16")
+
+
+def from_bits(bits, dtype: str):
+    """Raw 16-bit patterns of ``dtype`` ("f16" or "bf16") as fp32 values."""
+
+    b = np.asarray(bits, np.uint16)
+    if dtype == "f16":
+        return b.view(np.float16).astype(np.float32)
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def load_prologue_case(name: str) -> dict:
+    with np.load(GOLDEN_DIR / f"prologue_{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+def within_ulps(actual, expected, dtype: str, ulps: int = 1, rotated: bool = False) -> np.ndarray:
+    """Elementwise: |actual - expected| is at most ``ulps`` units in the last
+    place of ``dtype`` at the larger magnitude (or both equal, NaN included).
+    ``rotated``: the values are RoPE outputs over the last axis."""
+
+    a, e = np.asarray(actual, np.float64), np.asarray(expected, np.float64)
+    mag = np.maximum(np.abs(a), np.abs(e))
+    if rotated:
+        # A rotated element is x*cos + partner*sin, partner = column c ^ D/2:
+        # its rounding error scales with the larger of the two, not with the
+        # (possibly cancelled) result.
+        d = e.shape[-1]
+        mag = np.maximum(mag, np.abs(e[..., np.arange(d) ^ (d // 2)]))
+    mant = 10 if dtype == "f16" else 7
+    ulp = np.where(mag > 0, 2.0 ** (np.floor(np.log2(np.maximum(mag, 1e-30))) - mant), 2.0 ** -24)
+    ulp = np.maximum(ulp, 2.0 ** -24 if dtype == "f16" else 2.0 ** -133)
+    return (np.abs(a - e) <= ulps * ulp) | (a == e) | (np.isnan(a) & np.isnan(e))

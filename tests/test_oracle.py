@@ -281,3 +281,58 @@ def test_padding_rows_are_zero_and_empty_visibility_is_nan() -> None:
     )
     out = paged_attention(q, q, q, cache, md)
     assert np.all(np.isfinite(out[0])) and np.all(np.isnan(out[1])) and np.all(out[2] == 0)
+
+
+# ---------------------------------------------------------------- Qwen3 attention prologue
+from _golden import PROLOGUE_CASES, from_bits, load_prologue_case, within_ulps  # noqa: E402
+from oracle.qk_prologue import inverse_frequencies, qk_norm_rope_and_cache, rms_norm, rope  # noqa: E402
+
+
+@pytest.mark.parametrize("name", PROLOGUE_CASES)
+def test_prologue_oracle_matches_reference_golden(name: str) -> None:
+    """q/k RMSNorm + RoPE + KV write against the reference's own modules
+    (tests/golden/make_golden_prologue.py): every element within two ulps of
+    the model dtype (the variance is summed in another order, and a one-ulp
+    change of the normalised value can pass through the weight multiply and
+    the rotation), all but a handful exactly equal."""
+
+    z = load_prologue_case(name)
+    dt = str(z["dtype"])
+    q, k, v = (from_bits(z[n], dt) for n in ("query", "key", "value"))
+    cache = from_bits(z["cache_before"], dt).copy()
+    out = qk_norm_rope_and_cache(
+        q, k, v, z["positions"], from_bits(z["q_weight"], dt), from_bits(z["k_weight"], dt),
+        float(z["eps"]), z["inv_freq"], cache, z["slot_mapping"], dt,
+    )
+    expected_q, expected_cache = from_bits(z["q_out"], dt), from_bits(z["cache_after"], dt)
+    assert within_ulps(out, expected_q, dt, 2, rotated=True).all()
+    assert np.mean(out != expected_q) < 1e-3
+    assert within_ulps(cache, expected_cache, dt, 2, rotated=True).all()
+    # numpy's float32 power may differ from torch's by an ulp, which is why
+    # the kernel takes the inverse frequencies computed with torch exactly as
+    # the reference computes them (rotary_embedding.py:29-38).
+    np.testing.assert_allclose(inverse_frequencies(128, float(z["base"])), z["inv_freq"], rtol=3e-7)
+
+
+def test_prologue_rms_norm_kat() -> None:
+    """normalization test: fp16 [512, -384, 256, -128] equals the fp32
+    formula rounded to fp16 (tests/layers/test_normalization.py:16-33)."""
+
+    x = np.array([[[512.0, -384.0, 256.0, -128.0]]], np.float32)
+    eps = 1e-6
+    expected = (x * (1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps))).astype(np.float16)
+    out = rms_norm(x, np.ones(4, np.float32), eps, "f16")
+    np.testing.assert_array_equal(out, expected.astype(np.float32))
+
+
+def test_prologue_rope_is_a_rotation_of_half_pairs() -> None:
+    """RoPE rotates each pair (x_i, x_{i+D/2}) by pos * inv_freq_i (the
+    transformers comparison of tests/layers/test_rotary_embedding.py:35-52)."""
+
+    pos = np.array([5, 1, 127])
+    x = np.linspace(-1.0, 1.0, 3 * 4 * 8, dtype=np.float32).reshape(3, 4, 8)
+    inv = inverse_frequencies(8, 50_000.0)
+    out = rope(pos, x, inv, "f32")
+    z = (x[..., :4] + 1j * x[..., 4:]) * np.exp(1j * (pos[:, None, None] * inv[None, None, :]))
+    np.testing.assert_allclose(out[..., :4], z.real, atol=1e-6)
+    np.testing.assert_allclose(out[..., 4:], z.imag, atol=1e-6)
