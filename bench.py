@@ -27,7 +27,9 @@ Other workloads (parity and supplementary lines, not the default):
 ``--workload llama8b`` is BASELINE config 4 (32/8 heads, 64 seqs/GPU, ctx
 U[4096,8192], bf16) with the same metric; ``--workload mixed`` is config 3
 (8 chunked prefills of 2048 tokens over cached prefixes + 120 decodes, bf16)
-and reports the prefill kernel's tensor throughput in TFLOP/s.
+and reports the prefill kernel's tensor throughput in TFLOP/s; ``--workload
+prologue`` times the fused Qwen3 q/k-norm + RoPE + KV-write kernel on one
+8192-token step (config 5's max_num_batched_tokens) in GB/s.
 """
 
 from __future__ import annotations
@@ -102,7 +104,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b", "prologue"), default="decode",
                     help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
@@ -600,12 +602,91 @@ def run_mixed(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- prologue
+def run_prologue(args) -> None:
+    """Fused q/k RMSNorm + RoPE + KV write (mvb_qk_norm_rope_and_cache) on an
+    8192-token step at the Qwen3-0.6B attention shape, fp16 unless --dtype."""
+
+    import numpy as np
+    import torch
+
+    from micro_vllm_b200 import AttentionMetadata, qk_norm_rope_and_write, rotary_inverse_frequencies
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    tokens, hq, hkv, d, bs = 8192, NUM_Q_HEADS, NUM_KV_HEADS, HEAD_DIM, BLOCK_SIZE
+    g = torch.Generator(device=dev).manual_seed(7)
+    qkv = torch.randn((tokens, (hq + 2 * hkv) * d), generator=g, device=dev).to(dtype)
+    q = qkv[:, : hq * d].view(tokens, hq, d)
+    k = qkv[:, hq * d : (hq + hkv) * d].view(tokens, hkv, d)
+    v = qkv[:, (hq + hkv) * d :].view(tokens, hkv, d)
+    nb = int((args.pool_gb or 8.0) * 1e9) // (2 * bs * hkv * d * 2)
+    cache = torch.empty((2, nb, bs, hkv, d), dtype=dtype, device=dev)
+    slots = torch.randperm(nb * bs, generator=g, device=dev)[:tokens]
+    positions = torch.randint(0, 8192, (tokens,), generator=g, device=dev)
+    q_w = (0.5 + torch.rand(d, generator=g, device=dev)).to(dtype)
+    k_w = (0.5 + torch.rand(d, generator=g, device=dev)).to(dtype)
+    inv = rotary_inverse_frequencies(d, 1e6, dev)
+    md = AttentionMetadata(
+        query_positions=positions, query_context_start_positions=positions * 0,
+        query_start_locations=torch.tensor([0, tokens], device=dev),
+        context_lengths=torch.tensor([1], device=dev),
+        block_table=torch.zeros((1, 1), dtype=torch.int64, device=dev), slot_mapping=slots, block_size=bs,
+    )
+    step = lambda: qk_norm_rope_and_write(q, k, v, positions, q_w, k_w, 1e-6, inv, cache, md)  # noqa: E731
+    stream = torch.cuda.current_stream(dev)
+    # The step's 134 MB barely exceeds the 126 MB L2: evict it between steps
+    # by reading a 256 MB buffer (a read leaves no dirty lines to write back
+    # during the timed kernel, as a write-based flush would).
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    total = 0.0
+    for _ in range(args.steps):
+        flush.max()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        total += a.elapsed_time(b)
+    clock_info = clocks.stop()
+    ms = total / args.steps
+    rows = hq + 2 * hkv
+    byts = 2 * tokens * rows * d * 2  # read q, k, v; write q_out, k, v
+    achieved = byts / (ms * 1e-3) / 1e9
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peak, peak_src = 6650.0, "fallback"
+    if peaks_path.exists():
+        peak, peak_src = float(json.loads(peaks_path.read_text())["hbm_gbs"]), "measured"
+    line = {
+        "metric": "qk_norm_rope_cache_GBps", "value": achieved, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dtype == torch.float16 else "bf16",
+        "data": "synthetic",
+        "config": {"workload": "fused Qwen3 attention prologue: q/k RMSNorm + RoPE + KV write, "
+                               f"{tokens} tokens, 16/8/128, random slots over a {nb}-block pool",
+                   "l2": "L2 evicted (256 MB read) before every timed step"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "kernel": "qk_prologue_kernel", "bytes_per_launch": byts},
+        "gpu_launches": args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "mixed":
         run_mixed(args)
+    elif args.workload == "prologue":
+        run_prologue(args)
     else:
         run_ours(args)
 

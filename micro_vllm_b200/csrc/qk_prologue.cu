@@ -14,10 +14,11 @@
 // precomputed (the caller evaluates the reference's own expression), so the
 // angles are the reference's bit for bit.
 //
-// One warp per (token, group of up to 8 rows), rows being the token's Hq
-// query heads, then its Hkv key heads, then its Hkv value heads; a lane owns
-// 4 consecutive elements of the 128-element row, so rotate_half's partner of
-// lane l is lane l ^ 16.  All rows of a warp are loaded before any is used.
+// One warp per token: it evaluates the token's rotation angles once, then
+// walks its rows — the Hq query heads, the Hkv key heads, the Hkv value
+// heads — in batches of 8 loaded together.  A lane owns 4 consecutive
+// elements of the 128-element row, so rotate_half's partner of lane l is
+// lane l ^ 16.
 // Roofline: HBM; bytes per token = (Hq + 2 Hkv) * D * elsize read +
 // (Hq + 2 Hkv) * D * elsize written.
 #include <cuda_bf16.h>
@@ -101,43 +102,20 @@ template <typename T>
 __global__ void __launch_bounds__(32 * kPrologueWarps)
     qk_prologue_kernel(const PrologueParams p) {
   const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kPrologueWarps + (threadIdx.x >> 5);
+  if (t >= p.num_tokens) return;
   const int rows = p.num_q_heads + 2 * p.num_kv_heads;
-  const int groups = (rows + kRowsPerWarp - 1) / kRowsPerWarp;
-  const int64_t gw = (int64_t)blockIdx.x * kPrologueWarps + (threadIdx.x >> 5);
-  if (gw >= p.num_tokens * groups) return;
-  const int64_t t = gw / groups;
-  const int r0 = (int)(gw % groups) * kRowsPerWarp;
-  const int nr = min(kRowsPerWarp, rows - r0);
   const int qk_rows = p.num_q_heads + p.num_kv_heads;
 
   const int64_t slot = __ldg(p.slots + t);
   const bool write = slot >= 0 && slot < p.num_slots;
-  if (slot >= p.num_slots && r0 == 0 && lane == 0 && p.status != nullptr)
+  if (slot >= p.num_slots && lane == 0 && p.status != nullptr)
     atomicOr(p.status, MVB_STATUS_SLOT_OUT_OF_RANGE);
 
-  // Every row of the group in flight at once.
-  uint2 raw[kRowsPerWarp];
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    raw[i] = make_uint2(0, 0);
-    if (i < nr) {
-      const int r = r0 + i;
-      const char* base;
-      if (r < p.num_q_heads)
-        base = p.q + (t * p.q_st + (int64_t)r * p.q_sh) * 2;
-      else if (r < qk_rows)
-        base = p.k + (t * p.k_st + (int64_t)(r - p.num_q_heads) * p.k_sh) * 2;
-      else
-        base = p.v + (t * p.v_st + (int64_t)(r - qk_rows) * p.v_sh) * 2;
-      raw[i] = __ldg(reinterpret_cast<const uint2*>(base) + lane);
-    }
-  }
-
-  // Rotation of this lane's columns 4*lane..4*lane+3: column c and c + 64
-  // share frequency c mod 64 (angles = cat(freqs, freqs)).
-  float cs[4], sn[4];
-  float qw[4], kw[4];
-  if (r0 < qk_rows) {
+  // Rotation of this lane's columns 4*lane..4*lane+3, once per token:
+  // column c and c + 64 share frequency c mod 64 (angles = cat(freqs, freqs)).
+  float cs[4], sn[4], qw[4], kw[4];
+  {
     const float pf = (float)__ldg(p.pos + t);  // positions.to(float32)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -148,47 +126,67 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
     unpack4<T>(__ldg(reinterpret_cast<const uint2*>(p.k_w) + lane), kw);
   }
 
+  for (int r0 = 0; r0 < rows; r0 += kRowsPerWarp) {
+    const int nr = min(kRowsPerWarp, rows - r0);
+    // A batch of rows in flight at once.
+    uint2 raw[kRowsPerWarp];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    if (i >= nr) break;
-    const int r = r0 + i;
-    if (r >= qk_rows) {  // value row: straight into plane 1
-      if (write) {
-        char* dst = p.cache + ((p.num_slots + slot) * p.num_kv_heads + (r - qk_rows)) *
-                                  (int64_t)kPrologueDim * 2;
-        reinterpret_cast<uint2*>(dst)[lane] = raw[i];
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      raw[i] = make_uint2(0, 0);
+      if (i < nr) {
+        const int r = r0 + i;
+        const char* base;
+        if (r < p.num_q_heads)
+          base = p.q + (t * p.q_st + (int64_t)r * p.q_sh) * 2;
+        else if (r < qk_rows)
+          base = p.k + (t * p.k_st + (int64_t)(r - p.num_q_heads) * p.k_sh) * 2;
+        else
+          base = p.v + (t * p.v_st + (int64_t)(r - qk_rows) * p.v_sh) * 2;
+        raw[i] = __ldg(reinterpret_cast<const uint2*>(base) + lane);
       }
-      continue;
     }
-    const bool is_q = r < p.num_q_heads;
-    float x[4];
-    unpack4<T>(raw[i], x);
-    // RMSNorm: mean of squares over the row, fp32.
-    float ss = x[0] * x[0];
-    ss = __fadd_rn(ss, __fmul_rn(x[1], x[1]));
-    ss = __fadd_rn(ss, __fmul_rn(x[2], x[2]));
-    ss = __fadd_rn(ss, __fmul_rn(x[3], x[3]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    const float inv_rms = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / kPrologueDim), p.eps));
-    float y[4];
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      if (i >= nr) break;
+      const int r = r0 + i;
+      if (r >= qk_rows) {  // value row: straight into plane 1
+        if (write) {
+          char* dst = p.cache + ((p.num_slots + slot) * p.num_kv_heads + (r - qk_rows)) *
+                                    (int64_t)kPrologueDim * 2;
+          reinterpret_cast<uint2*>(dst)[lane] = raw[i];
+        }
+        continue;
+      }
+      const bool is_q = r < p.num_q_heads;
+      float x[4];
+      unpack4<T>(raw[i], x);
+      // RMSNorm: mean of squares over the row, fp32.
+      float ss = x[0] * x[0];
+      ss = __fadd_rn(ss, __fmul_rn(x[1], x[1]));
+      ss = __fadd_rn(ss, __fmul_rn(x[2], x[2]));
+      ss = __fadd_rn(ss, __fmul_rn(x[3], x[3]));
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      y[e] = rnd<T>(__fmul_rn(is_q ? qw[e] : kw[e], rnd<T>(__fmul_rn(x[e], inv_rms))));
-    // rotate_half: the first half takes -x[c + 64], the second x[c - 64].
-    float out[4];
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      const float inv_rms = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / kPrologueDim), p.eps));
+      float y[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
-      const float rot = lane < 16 ? -partner : partner;
-      out[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(rot, sn[e]));
-    }
-    const uint2 w = pack4<T>(out);
-    if (is_q) {
-      reinterpret_cast<uint2*>(p.q_out + ((t * p.num_q_heads + r) * (int64_t)kPrologueDim) * 2)[lane] = w;
-    } else if (write) {
-      char* dst = p.cache + (slot * p.num_kv_heads + (r - p.num_q_heads)) * (int64_t)kPrologueDim * 2;
-      reinterpret_cast<uint2*>(dst)[lane] = w;
+      for (int e = 0; e < 4; ++e)
+        y[e] = rnd<T>(__fmul_rn(is_q ? qw[e] : kw[e], rnd<T>(__fmul_rn(x[e], inv_rms))));
+      // rotate_half: the first half takes -x[c + 64], the second x[c - 64].
+      float out[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
+        const float rot = lane < 16 ? -partner : partner;
+        out[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(rot, sn[e]));
+      }
+      const uint2 w = pack4<T>(out);
+      if (is_q) {
+        reinterpret_cast<uint2*>(p.q_out + ((t * p.num_q_heads + r) * (int64_t)kPrologueDim) * 2)[lane] = w;
+      } else if (write) {
+        char* dst = p.cache + (slot * p.num_kv_heads + (r - p.num_q_heads)) * (int64_t)kPrologueDim * 2;
+        reinterpret_cast<uint2*>(dst)[lane] = w;
+      }
     }
   }
 }
@@ -229,9 +227,7 @@ int launch_qk_prologue(const QkPrologueArgs& a) {
   p.num_q_heads = a.num_q_heads;
   p.num_kv_heads = a.num_kv_heads;
   p.status = a.status;
-  const int rows = a.num_q_heads + 2 * a.num_kv_heads;
-  const int64_t warps = a.num_tokens * ((rows + kRowsPerWarp - 1) / kRowsPerWarp);
-  const int64_t blocks = (warps + kPrologueWarps - 1) / kPrologueWarps;
+  const int64_t blocks = (a.num_tokens + kPrologueWarps - 1) / kPrologueWarps;
   if (blocks > INT32_MAX) return MVB_ERR_UNSUPPORTED_SHAPE;
   if (a.dtype == MVB_DTYPE_BF16)
     qk_prologue_kernel<__nv_bfloat16><<<(unsigned)blocks, 32 * kPrologueWarps, 0, a.stream>>>(p);
