@@ -160,24 +160,6 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// ------------------------------------------------------------ helpers
-// Physical page of logical position `pos`, or -1 when the table has no
-// valid entry for it.
-__device__ __forceinline__ int64_t page_of(const DecodeParams& p, const int64_t* trow, int64_t pos,
-                                           int64_t* offset) {
-  int64_t lb;
-  if (p.bs_shift >= 0) {
-    lb = pos >> p.bs_shift;
-    *offset = pos & (p.block_size - 1);
-  } else {
-    lb = pos / p.block_size;
-    *offset = pos - lb * p.block_size;
-  }
-  if (pos < 0 || lb >= p.table_width) return -1;
-  const int64_t blk = __ldg(trow + lb);
-  return (blk >= 0 && blk < p.num_blocks) ? blk : -1;
-}
-
 // The visible KV extent of request r: [lo, hi) and its tile origin.
 struct Extent {
   int64_t qs, lo, hi, base;
@@ -234,6 +216,22 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
       e = extent_of(p, r);
       trow = p.table + r * p.table_stride;
     }
+    // The page lookup (a global load) goes out before the wait for a free
+    // stage, so its latency overlaps the wait.
+    const int64_t tile = local - req_lo;
+    const int64_t pos = e.base + tile * kTile + row;
+    int64_t off, lb;
+    if (p.bs_shift >= 0) {
+      lb = pos >> p.bs_shift;
+      off = pos & (p.block_size - 1);
+    } else {
+      lb = pos / p.block_size;
+      off = pos - lb * p.block_size;
+    }
+    // -2: outside the visible extent; -1: outside the table.
+    const bool in_extent = pos >= e.lo && pos < e.hi;
+    const bool in_table = pos >= 0 && lb < p.table_width;
+    const int64_t raw_blk = in_extent && in_table ? __ldg(trow + lb) : 0;  // checked after the wait
     const int s = k % kStages;
     if (!mbar_wait(empty0 + 8 * s, ((k / kStages) & 1) ^ 1, p.status)) {
       // A consumer stopped: let the copies already issued land before the
@@ -242,10 +240,8 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
         mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, nullptr);
       return;
     }
-    const int64_t tile = local - req_lo;
-    const int64_t pos = e.base + tile * kTile + row;
-    int64_t off = 0;
-    const int64_t blk = (pos >= e.lo && pos < e.hi) ? page_of(p, trow, pos, &off) : -2;
+    const int64_t blk = !in_extent ? -2
+                        : (in_table && raw_blk >= 0 && raw_blk < p.num_blocks) ? raw_blk : -1;
     const bool valid = blk >= 0;
     if (blk == -1 && p.status != nullptr) atomicOr(p.status, MVB_STATUS_BLOCK_OUT_OF_RANGE);
     const uint32_t mask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
