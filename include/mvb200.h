@@ -205,6 +205,31 @@ MVB_API int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strid
                                        int32_t num_q_heads, int32_t dtype, int32_t* status,
                                        void* stream);
 
+/*
+ * Batched token sampler: the next token of every logits row in one launch.
+ *
+ * Replaces the per-row loop of Sampler.__call__ / _sample_row with
+ * _apply_top_k and _apply_top_p (src/micro_vllm/sampling/sampler.py:14-87),
+ * which synchronises the host once per row.
+ *
+ * logits [num_rows, vocab] with row stride row_stride (elements, >= 0: rows
+ * may repeat), any MVB_DTYPE_*.  Per row (device arrays of num_rows): temperature (0 =
+ * greedy: the first index of the largest logit, as torch.argmax), top_k (<= 0
+ * or >= vocab: no filter), top_p (1 = no filter), seed and sample_index.
+ * A stochastic row divides the logits by the temperature in fp32, keeps the
+ * top_k largest (equal values at the cut: lowest indices first), then the
+ * shortest prefix of the descending order whose mass before each token is
+ * <= top_p, and draws one token in proportion to exp(x - max) with a
+ * uniform number from Philox4x32-10 keyed by seed with sample_index as the
+ * counter (the same pair always gives the same token; the stream differs
+ * from torch's generator).  out_tokens (device int64 [num_rows]) receives the
+ * token ids.  Nothing is allocated and the host is not synchronised.
+ */
+MVB_API int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
+                       int32_t dtype, const float* temperature, const int32_t* top_k,
+                       const float* top_p, const uint64_t* seed, const int64_t* sample_index,
+                       int64_t* out_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,7 +2,8 @@
 
 The hot path of micro-vLLM's attention-operator layer — the KV-cache scatter
 and paged attention over that cache, plus the fused q/k-norm + RoPE + KV-write
-prologue of a Qwen3 layer — as hand-written CUDA behind a C ABI
+prologue of a Qwen3 layer, and a batched device sampler — as hand-written
+CUDA behind a C ABI
 (include/mvb200.h, ``libmvb200.so``), with a Python operator that mirrors
 the reference's ``AttentionOperator`` interface.
 """
@@ -28,6 +29,7 @@ from micro_vllm_b200.prologue import (  # noqa: F401
     qk_norm_rope_and_write,
     rotary_inverse_frequencies,
 )
+from micro_vllm_b200.sampling import B200Sampler, sample_tokens  # noqa: F401
 
 __all__ = [
     "Attention",
@@ -35,6 +37,7 @@ __all__ = [
     "AttentionOperator",
     "AttentionSpec",
     "B200PagedAttentionOperator",
+    "B200Sampler",
     "ChunkedLocalSpec",
     "FullAttentionSpec",
     "OPERATOR_NAME",
@@ -44,5 +47,6 @@ __all__ = [
     "map_cache_slots",
     "qk_norm_rope_and_write",
     "rotary_inverse_frequencies",
+    "sample_tokens",
     "write_kv_cache",
 ]

@@ -72,6 +72,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _P, _I64, _I32, _I32, _P, _P,  # slots, T, Hq, dtype, status, stream
         ],
     ),
+    "mvb_sample": (
+        ctypes.c_int,
+        [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _P],
+    ),
     "mvb_attention_forward": (
         ctypes.c_int,
         [

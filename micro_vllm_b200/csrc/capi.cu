@@ -204,4 +204,30 @@ int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strides, cons
   return launch_qk_prologue(a);
 }
 
+int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
+               int32_t dtype, const float* temperature, const int32_t* top_k, const float* top_p,
+               const uint64_t* seed, const int64_t* sample_index, int64_t* out_tokens,
+               void* stream) {
+  if (elem_bytes_of(dtype) == 0) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_rows < 0 || vocab <= 0 || vocab >= ((int64_t)1 << 31) || row_stride < 0)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return MVB_OK;
+  if (!logits || !temperature || !top_k || !top_p || !seed || !sample_index || !out_tokens)
+    return MVB_ERR_INVALID_ARGUMENT;
+  SampleArgs a;
+  a.logits = logits;
+  a.row_stride = row_stride;
+  a.num_rows = num_rows;
+  a.vocab = vocab;
+  a.dtype = dtype;
+  a.temperature = temperature;
+  a.top_k = top_k;
+  a.top_p = top_p;
+  a.seed = seed;
+  a.sample_index = sample_index;
+  a.out_tokens = out_tokens;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_sample(a);
+}
+
 }  // extern "C"

@@ -118,6 +118,20 @@ struct QkPrologueArgs {
 };
 int launch_qk_prologue(const QkPrologueArgs& a);
 
+struct SampleArgs {
+  const void* logits;
+  int64_t row_stride, num_rows, vocab;
+  int32_t dtype;
+  const float* temperature;
+  const int32_t* top_k;
+  const float* top_p;
+  const uint64_t* seed;
+  const int64_t* sample_index;
+  int64_t* out_tokens;
+  cudaStream_t stream;
+};
+int launch_sample(const SampleArgs& a);
+
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,
                 int32_t decode_ctas, int32_t prefill_block_q);
 int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w, int32_t grid,

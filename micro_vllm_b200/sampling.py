@@ -1,0 +1,114 @@
+"""Batched device sampler (``mvb_sample``): the next token of every row at once.
+
+The reference samples row by row (src/micro_vllm/sampling/sampler.py:14-61),
+each row ending in ``.item()`` — one host synchronisation per request per
+step.  ``B200Sampler`` keeps the same call signature and per-row policy
+(greedy argmax; temperature, top-k, top-p, seeded multinomial) and runs all
+rows in one kernel; the host reads the token ids once.  ``sample_tokens``
+returns them on the device without any synchronisation.
+
+The uniform draws come from the kernel's own Philox4x32-10 stream keyed by
+the row's seed with its sample index as the counter: a (seed, sample index)
+pair always gives the same token, independently of the other rows, but not
+the token torch's generator would give.
+"""
+
+from __future__ import annotations
+
+import secrets
+from dataclasses import dataclass
+
+import torch
+
+from micro_vllm_b200 import _lib
+from micro_vllm_b200.operators import _DTYPES
+
+
+@dataclass(frozen=True, slots=True)
+class SampledToken:
+    """Mirror of the reference's SampledToken (executor/interface.py)."""
+
+    request_id: str
+    token_id: int
+
+
+@dataclass(frozen=True, slots=True)
+class SamplerOutput:
+    """Mirror of the reference's ModelRunnerOutput (executor/interface.py)."""
+
+    sampled_tokens: tuple[SampledToken, ...] = ()
+
+
+def sample_tokens(
+    logits: torch.Tensor,
+    temperature: torch.Tensor,
+    top_k: torch.Tensor,
+    top_p: torch.Tensor,
+    seed: torch.Tensor,
+    sample_index: torch.Tensor,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Token ids (device int64 [rows]) for ``logits`` [rows, vocab].
+
+    Per-row device tensors: ``temperature`` float32 (0: greedy), ``top_k``
+    int32 (<= 0: none), ``top_p`` float32 (1: none), ``seed`` int64 (used as
+    an unsigned 64-bit key) and ``sample_index`` int64."""
+
+    if logits.device.type != "cuda":
+        raise RuntimeError("b200_paged sampler requires CUDA tensors")
+    dtype = _DTYPES.get(logits.dtype)
+    if dtype is None:
+        raise ValueError("b200_paged sampler supports float16, bfloat16 and float32 logits")
+    if logits.dim() != 2:
+        raise ValueError("logits must be [rows, vocab]")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    rows, vocab = logits.shape
+    dev = logits.device
+    expect = ((temperature, torch.float32), (top_k, torch.int32), (top_p, torch.float32),
+              (seed, torch.int64), (sample_index, torch.int64))
+    for t, dt in expect:
+        if t.dtype != dt or t.shape != (rows,) or t.device != dev:
+            raise ValueError(f"per-row sampling tensors must be {dt} [{rows}] on {dev}")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=dev)
+    if rows == 0:
+        return out
+    lib = _lib.load()
+    rc = lib.mvb_sample(
+        logits.data_ptr(), logits.stride(0), rows, vocab, dtype,
+        temperature.contiguous().data_ptr(), top_k.contiguous().data_ptr(),
+        top_p.contiguous().data_ptr(), seed.contiguous().data_ptr(),
+        sample_index.contiguous().data_ptr(), out.data_ptr(),
+        torch.cuda.current_stream(dev).cuda_stream,
+    )
+    _lib.check(rc, "b200_paged sampler")
+    return out
+
+
+class B200Sampler:
+    """``Sampler.__call__(logits, request_ids, sampling_params, sample_indices)``
+    (sampler.py:14-37) with every row sampled in one launch.  Accepts the
+    reference's SamplingParams (or anything with ``temperature``, ``top_k``,
+    ``top_p`` and ``seed``); a row without a seed gets a random one, as the
+    reference draws ``secrets.randbits(63)`` (sampler.py:51-53)."""
+
+    __slots__ = ()
+
+    def __call__(self, logits, request_ids, sampling_params, sample_indices, /) -> SamplerOutput:
+        rows = len(request_ids)
+        if rows == 0:
+            return SamplerOutput()
+        dev = logits.device
+        temperature = torch.tensor([float(p.temperature) for p in sampling_params], dtype=torch.float32)
+        top_k = torch.tensor([0 if p.top_k is None else int(p.top_k) for p in sampling_params],
+                             dtype=torch.int32)
+        top_p = torch.tensor([float(p.top_p) for p in sampling_params], dtype=torch.float32)
+        seed = torch.tensor(
+            [(p.seed if p.seed is not None else secrets.randbits(63)) for p in sampling_params],
+            dtype=torch.int64,
+        )
+        index = torch.tensor([int(i) for i in sample_indices], dtype=torch.int64)
+        packed = [t.to(dev, non_blocking=True) for t in (temperature, top_k, top_p, seed, index)]
+        tokens = sample_tokens(logits, *packed).cpu()  # the one host read of the step
+        return SamplerOutput(tuple(SampledToken(r, int(t)) for r, t in zip(request_ids, tokens)))

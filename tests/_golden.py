@@ -87,3 +87,14 @@ def within_ulps(actual, expected, dtype: str, ulps: int = 1, rotated: bool = Fal
     ulp = np.where(mag > 0, 2.0 ** (np.floor(np.log2(np.maximum(mag, 1e-30))) - mant), 2.0 ** -24)
     ulp = np.maximum(ulp, 2.0 ** -24 if dtype == "f16" else 2.0 ** -133)
     return (np.abs(a - e) <= ulps * ulp) | (a == e) | (np.isnan(a) & np.isnan(e))
+
+
+# ---------------------------------------------------------------- sampler
+SAMPLER_TIE_ROW = 2  # two equal maxima: the filters' tie order is left open by torch
+
+
+def load_sampler_cases() -> dict:
+    with np.load(GOLDEN_DIR / "sampler_cases.npz") as z:
+        d = {k: z[k] for k in z.files}
+    d["kept"] = np.unpackbits(d["kept"], axis=-1)[..., : d["logits"].shape[1]].astype(bool)
+    return d

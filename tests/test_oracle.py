@@ -336,3 +336,37 @@ def test_prologue_rope_is_a_rotation_of_half_pairs() -> None:
     z = (x[..., :4] + 1j * x[..., 4:]) * np.exp(1j * (pos[:, None, None] * inv[None, None, :]))
     np.testing.assert_allclose(out[..., :4], z.real, atol=1e-6)
     np.testing.assert_allclose(out[..., 4:], z.imag, atol=1e-6)
+
+
+# ---------------------------------------------------------------- sampler
+from _golden import SAMPLER_TIE_ROW, load_sampler_cases  # noqa: E402
+from oracle.sampler import greedy, kept_and_probabilities  # noqa: E402
+
+
+def test_sampler_oracle_matches_reference_golden() -> None:
+    """Greedy tokens (ties: first index) and the sets top-k / top-p keep,
+    against the reference's Sampler and filters (make_golden_sampler.py)."""
+
+    z = load_sampler_cases()
+    assert [greedy(r) for r in z["logits"]] == z["greedy"].tolist()
+    for c in range(len(z["temperature"])):
+        k = int(z["top_k"][c])
+        for r, row in enumerate(z["logits"]):
+            kept, probs = kept_and_probabilities(row, float(z["temperature"][c]), k or None, float(z["top_p"][c]))
+            if r == SAMPLER_TIE_ROW:
+                assert kept.sum() == z["kept"][c, r].sum()
+            else:
+                np.testing.assert_array_equal(kept, z["kept"][c, r])
+            assert abs(probs.sum() - 1.0) < 1e-9 and np.all(probs[~kept] == 0)
+
+
+def test_sampler_oracle_reference_test_cases() -> None:
+    """sampler tests: top-p keeps the boundary token (test_sampler.py:127-143),
+    top-k keeps the largest (:96-111), top-k >= vocab filters nothing (:114-124)."""
+
+    kept, _ = kept_and_probabilities(np.array([3.0, 2.0, 0.0, -1.0]), 1.0, None, 0.8)
+    assert kept.tolist() == [True, True, False, False]
+    kept, _ = kept_and_probabilities(np.array([0.0, 1.0, 2.0, 3.0, 4.0]), 1.0, 2, 1.0)
+    assert kept.tolist() == [False, False, False, True, True]
+    kept, _ = kept_and_probabilities(np.array([0.0, 1.0, 2.0]), 1.0, 3, 1.0)
+    assert kept.all()
