@@ -29,7 +29,10 @@ U[4096,8192], bf16) with the same metric; ``--workload mixed`` is config 3
 (8 chunked prefills of 2048 tokens over cached prefixes + 120 decodes, bf16)
 and reports the prefill kernel's tensor throughput in TFLOP/s; ``--workload
 prologue`` times the fused Qwen3 q/k-norm + RoPE + KV-write kernel on one
-8192-token step (config 5's max_num_batched_tokens) in GB/s.
+8192-token step (config 5's max_num_batched_tokens) in GB/s; ``--workload
+sample`` the batched sampler on 256 rows of a 151936-token vocabulary (GB/s
+of logits); ``--workload metadata`` the device build of a config-2 step's
+metadata (us per step, lower is better).
 """
 
 from __future__ import annotations
@@ -104,7 +107,8 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b", "prologue"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b", "prologue", "sample", "metadata"),
+                    default="decode",
                     help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
@@ -679,6 +683,247 @@ def run_prologue(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _hbm_peak() -> tuple[float, str]:
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        return float(json.loads(peaks_path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- sampler
+def run_sample(args) -> None:
+    """Batched device sampler (mvb_sample): one token for each of 256 rows of a
+    151936-token vocabulary (Qwen3; one row per decode sequence of config 2),
+    bf16 logits unless --dtype; a quarter of the rows greedy, a quarter top-k
+    50, a quarter top-p 0.9, a quarter both, temperature 0.8."""
+
+    import numpy as np
+    import torch
+
+    from micro_vllm_b200 import sample_tokens
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
+    rows, vocab = BATCH_PER_GPU, 151936
+    g = torch.Generator(device=dev).manual_seed(9)
+    logits = (torch.randn((rows, vocab), generator=g, device=dev) * 2.0).to(dtype)
+    r = torch.arange(rows, device=dev)
+    temperature = torch.where(r % 4 == 0, 0.0, 0.8).float()
+    top_k = torch.where((r % 4 == 1) | (r % 4 == 3), 50, 0).int()
+    top_p = torch.where(r % 4 >= 2, 0.9, 1.0).float()
+    seed, index = r * 7 + 1, r.clone()
+    out = torch.empty(rows, dtype=torch.int64, device=dev)
+    step = lambda: sample_tokens(logits, temperature, top_k, top_p, seed, index, out=out)  # noqa: E731
+    stream = torch.cuda.current_stream(dev)
+    # 78 MB of logits fit in the 126 MB L2: evict them before every timed step
+    # by reading a 256 MB buffer.
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    total = 0.0
+    for _ in range(args.steps):
+        flush.max()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        total += a.elapsed_time(b)
+    clock_info = clocks.stop()
+    ms = total / args.steps
+    byts = rows * vocab * logits.element_size()
+    achieved = byts / (ms * 1e-3) / 1e9
+
+    # End to end: logits from pinned host memory, tokens back to the host.
+    host_logits = logits.cpu().pin_memory()
+    params = [t.cpu().pin_memory() for t in (temperature, top_k, top_p, seed, index)]
+    host_out = torch.empty(rows, dtype=torch.int64).pin_memory()
+    h2d = host_logits.numel() * host_logits.element_size() + sum(t.numel() * t.element_size() for t in params)
+
+    def e2e_step() -> None:
+        dl = host_logits.to(dev, non_blocking=True)
+        dp = [t.to(dev, non_blocking=True) for t in params]
+        host_out.copy_(sample_tokens(dl, *dp), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = a.elapsed_time(b) / args.steps
+
+    # CPU baseline: the oracle's row policy (numpy) on a bounded sample of rows.
+    from oracle.sampler import greedy, kept_and_probabilities
+
+    host = logits[:32].float().cpu().numpy()
+    rng = np.random.default_rng(0)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < min(args.cpu_sample_seconds, 10.0):
+        i = done % len(host)
+        if i % 4 == 0:
+            greedy(host[i])
+        else:
+            kept, probs = kept_and_probabilities(host[i], 0.8, 50 if i % 4 in (1, 3) else None,
+                                                 0.9 if i % 4 >= 2 else 1.0)
+            rng.choice(vocab, p=probs)
+        done += 1
+    cpu_s = time.perf_counter() - t0
+    peak, peak_src = _hbm_peak()
+    line = {
+        "metric": "sampler_logits_GBps", "value": achieved, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f16",
+        "data": "synthetic",
+        "config": {"workload": f"batched sampler: {rows} rows x {vocab} vocab, greedy / top-k 50 / top-p 0.9 / "
+                               "both, temperature 0.8, Philox draws",
+                   "rows_per_s": rows / (ms * 1e-3),
+                   "l2": "L2 evicted (256 MB read) before every timed step"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "kernel": "sample_kernel", "bytes_per_launch": byts},
+        "e2e": {"value": byts / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": rows * 8, "ms_per_step": e2e_ms},
+        "cpu_baseline": {"value": done * vocab * logits.element_size() / cpu_s / 1e9, "unit": "GB/s", "cores": 1,
+                         "kind": "port",
+                         "sample": f"{done} rows of the same logits through oracle/sampler.py (numpy) in "
+                                   f"{cpu_s:.1f}s, {cpu_s / done * 1e3:.2f} ms/row"},
+        "gpu_launches": args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- metadata
+def run_metadata(args) -> None:
+    """Device-side metadata build (mvb_build_metadata) of a config-2 step: 256
+    decode requests, ctx U[512,4096], block size 16, one full-attention cache
+    group, block ids drawn without replacement from an 80%-of-HBM pool."""
+
+    import numpy as np
+    import torch
+
+    from micro_vllm_b200 import DeviceMetadataBuilder, FullAttentionSpec, _lib
+    from oracle.metadata import PlannedRequest
+    from oracle.metadata import build as oracle_build
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    shape = DecodeShape(args)
+    ctx = shape.lengths(shape.batch, seed=1000)
+    pool = 2_340_000
+    rng = np.random.default_rng(4)
+    perm = iter(rng.permutation(pool - 1).tolist())
+
+    class _Req:
+        __slots__ = ("request_id", "input_token_ids", "num_computed_tokens", "num_scheduled_tokens",
+                     "requires_sampling", "block_tables")
+
+    class _Blocks:
+        __slots__ = ("block_ids",)
+
+    reqs = []
+    for i, c in enumerate(ctx):
+        q, b = _Req(), _Blocks()
+        b.block_ids = tuple(next(perm) for _ in range(-(-c // BLOCK_SIZE)))
+        q.request_id, q.input_token_ids = f"seq{i}", (int(rng.integers(0, 151936)),)
+        q.num_computed_tokens, q.num_scheduled_tokens, q.requires_sampling = c - 1, 1, True
+        q.block_tables = (b,)
+        reqs.append(q)
+
+    class _Plan:
+        scheduled_requests = tuple(reqs)
+
+    plan = _Plan()
+    builder = DeviceMetadataBuilder([FullAttentionSpec()], BLOCK_SIZE, pool - 1, dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        builder.build(plan)
+    torch.cuda.synchronize(dev)
+
+    # Kernel alone: the packed plan already on the device, the launches
+    # replayed from a CUDA graph so that the host's launch cost stays out.
+    staged = builder.stage(plan)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        builder.launch(staged)  # warm the graph pool's allocations
+    torch.cuda.synchronize(dev)
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            step = builder.launch(staged)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    kern_us = a.elapsed_time(b) / args.steps * 1e3
+    del graph
+
+    # End to end through the public call: pack + one upload + launch, and a
+    # read of the step's last slot back to the host (a synchronisation).
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step = builder.build(plan)
+        int(step.layer_attention_metadata[0].slot_mapping[-1])
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    clock_info = clocks.stop()
+    e2e_us = a.elapsed_time(b) / args.steps * 1e3
+    assert builder.read_status() == 0
+
+    r, t = len(reqs), len(reqs)
+    w = max(-(-c // BLOCK_SIZE) for c in ctx)
+    nblk = sum(-(-c // BLOCK_SIZE) for c in ctx)
+    byts = staged.bytes + 8 * (4 * t + 2 * r + 1 + r * w + r)  # inputs read; int64 outputs written
+
+    planned = [PlannedRequest(q.input_token_ids, q.num_computed_tokens, 1, True, (q.block_tables[0].block_ids,))
+               for q in reqs]
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < min(args.cpu_sample_seconds, 5.0):
+        oracle_build(planned, BLOCK_SIZE, pool - 1, [("full", 0)])
+        calls += 1
+    cpu_us = (time.perf_counter() - t0) / calls * 1e6
+    peak, peak_src = _hbm_peak()
+    achieved = byts / (kern_us * 1e-6) / 1e9
+    line = {
+        "metric": "metadata_build_us", "value": kern_us, "unit": "us/step", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": kern_us / 1e3,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic",
+        "config": {"workload": f"metadata of a config-2 step: {r} decode requests, ctx {shape.ctx_label}, "
+                               f"{nblk} block ids, table {r}x{w}, one full-attention group",
+                   "l2": "inputs and outputs under 1 MB (L2-resident): a launch-latency-bound kernel"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_src, "kernel": "build_metadata_kernel",
+                     "bytes_per_launch": byts,
+                     "note": "a few-us kernel timed in a CUDA graph: bound by launch latency and one "
+                             "grid-wide pass over sub-MB data, not bandwidth"},
+        "e2e": {"value": e2e_us, "unit": "us/step", "h2d_bytes_per_step": staged.bytes, "d2h_bytes_per_step": 8,
+                "what": "DeviceMetadataBuilder.build(plan) from the plan's Python objects: host packing, one "
+                        "pinned upload, the launch, and a read back of the last slot"},
+        "cpu_baseline": {"value": cpu_us, "unit": "us/step", "cores": 1, "kind": "port",
+                         "sample": f"the whole step through oracle/metadata.py (numpy restatement of the "
+                                   f"reference's host build), {calls} calls"},
+        "gpu_launches": 2 * args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+    del step
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -687,6 +932,10 @@ def main() -> None:
         run_mixed(args)
     elif args.workload == "prologue":
         run_prologue(args)
+    elif args.workload == "sample":
+        run_sample(args)
+    elif args.workload == "metadata":
+        run_metadata(args)
     else:
         run_ours(args)
 

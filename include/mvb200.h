@@ -50,6 +50,13 @@ extern "C" {
 /* Bits OR-ed into the optional device status word by the kernels. */
 #define MVB_STATUS_SLOT_OUT_OF_RANGE 1   /* slot >= num_blocks*block_size: row skipped  */
 #define MVB_STATUS_BLOCK_OUT_OF_RANGE 2  /* block id outside [0,num_blocks): key hidden */
+#define MVB_STATUS_POSITION_PAST_TABLE 4 /* position past its request's block ids: slot -1 */
+#define MVB_STATUS_INCONSISTENT_COUNTS 8 /* counts disagree with the sizes: padding only */
+
+/* Visibility specs of mvb_build_metadata (attention/spec.py). */
+#define MVB_SPEC_FULL 0           /* FullAttentionSpec: start 0                          */
+#define MVB_SPEC_SLIDING_WINDOW 1 /* SlidingWindowSpec(param): max(0, pos - param + 1)  */
+#define MVB_SPEC_CHUNKED_LOCAL 2  /* ChunkedLocalSpec(param): (pos / param) * param     */
 
 /* Library version, (major << 16) | minor. */
 MVB_API int mvb_version(void);
@@ -216,19 +223,73 @@ MVB_API int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strid
  * may repeat), any MVB_DTYPE_*.  Per row (device arrays of num_rows): temperature (0 =
  * greedy: the first index of the largest logit, as torch.argmax), top_k (<= 0
  * or >= vocab: no filter), top_p (1 = no filter), seed and sample_index.
- * A stochastic row divides the logits by the temperature in fp32, keeps the
- * top_k largest (equal values at the cut: lowest indices first), then the
- * shortest prefix of the descending order whose mass before each token is
- * <= top_p, and draws one token in proportion to exp(x - max) with a
- * uniform number from Philox4x32-10 keyed by seed with sample_index as the
- * counter (the same pair always gives the same token; the stream differs
- * from torch's generator).  out_tokens (device int64 [num_rows]) receives the
- * token ids.  Nothing is allocated and the host is not synchronised.
+ * A stochastic row keeps the top_k largest of x = logit / temperature
+ * (equal values at the cut: lowest indices first; division by T > 0 is
+ * monotone, so tokens are ordered by the logit, which also orders equal x
+ * from different fp32 logits), then, in descending order, every token whose
+ * mass before it is <= top_p (masses exp(x - max) in 1.31 fixed point, so a
+ * token below 2^-31 of the max has none and sits below any top-p cut), and
+ * draws one token in proportion to its mass with a uniform number from
+ * Philox4x32-10 keyed by seed with sample_index as the counter (the same pair
+ * always gives the same token; the stream differs from torch's generator).
+ * out_tokens (device int64 [num_rows]) receives the token ids.  Nothing is
+ * allocated and the host is not synchronised.
  */
 MVB_API int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
                        int32_t dtype, const float* temperature, const int32_t* top_k,
                        const float* top_p, const uint64_t* seed, const int64_t* sample_index,
                        int64_t* out_tokens, void* stream);
+
+/*
+ * Device-side build of one step's attention metadata (one cache group).
+ *
+ * Replaces the host loops of ModelRunner._flatten_model_input,
+ * _build_slot_mapping and _build_block_table
+ * (src/micro_vllm/worker/model_runner.py:751-900), the per-position loop of
+ * Attention.build_metadata (src/micro_vllm/attention/attention.py:56-85) and
+ * map_cache_slots (attention.py:31-41); with capacities above the actual
+ * sizes it also pads as _CudaGraphExecution.copy_input does
+ * (model_runner.py:78-122).
+ *
+ * Inputs (device, per scheduled request in plan order, num_requests of them):
+ * num_computed_tokens, num_scheduled_tokens, num_block_ids (int32), the
+ * requests' block ids concatenated (int32, num_block_ids_total of them),
+ * requires_sampling (uint8, may be NULL when num_sampled is 0) and the
+ * concatenated input token ids (int32 [num_tokens], may be NULL when
+ * input_ids is NULL).  num_tokens, num_block_ids_total and num_sampled are
+ * the sums of the counts, below 2^31; num_requests <= 16384 (else
+ * MVB_ERR_UNSUPPORTED_SHAPE).
+ *
+ * Outputs (device int64, each may be NULL to skip it):
+ *   input_ids, positions, context_starts, slot_mapping [token_capacity]
+ *     (0, 0, 0, -1 past num_tokens); context_starts follow spec_kind /
+ *     spec_param (MVB_SPEC_*);
+ *   query_start_locations [request_capacity + 1] (num_tokens past
+ *     num_requests + 1), context_lengths [request_capacity] (0 past
+ *     num_requests);
+ *   block_table [request_capacity, table_width], row stride table_stride,
+ *     null_block_id past each request's block ids;
+ *   sampling_rows [num_sampled]: the last token of each request with
+ *     requires_sampling set.
+ * A position whose logical block lies past its request's block ids (the
+ * reference raises IndexError) gets slot -1 and sets
+ * MVB_STATUS_POSITION_PAST_TABLE; counts that are negative, do not sum to
+ * the sizes passed or exceed table_width leave padding only and set
+ * MVB_STATUS_INCONSISTENT_COUNTS.  One launch; the host is not synchronised.
+ */
+MVB_API int mvb_build_metadata(const int32_t* num_computed_tokens,
+                               const int32_t* num_scheduled_tokens, const int32_t* num_block_ids,
+                               const int32_t* block_ids, const uint8_t* requires_sampling,
+                               const int32_t* input_token_ids, int64_t num_requests,
+                               int64_t num_tokens, int64_t num_block_ids_total,
+                               int64_t num_sampled, int64_t request_capacity,
+                               int64_t token_capacity, int64_t table_width, int64_t table_stride,
+                               int32_t block_size, int64_t null_block_id, int32_t spec_kind,
+                               int64_t spec_param, int64_t* input_ids, int64_t* positions,
+                               int64_t* context_starts, int64_t* query_start_locations,
+                               int64_t* context_lengths, int64_t* block_table,
+                               int64_t* slot_mapping, int64_t* sampling_rows, int32_t* status,
+                               void* stream);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,12 @@ MVB_DTYPE_F32 = 2
 
 MVB_STATUS_SLOT_OUT_OF_RANGE = 1
 MVB_STATUS_BLOCK_OUT_OF_RANGE = 2
+MVB_STATUS_POSITION_PAST_TABLE = 4
+MVB_STATUS_INCONSISTENT_COUNTS = 8
+
+MVB_SPEC_FULL = 0
+MVB_SPEC_SLIDING_WINDOW = 1
+MVB_SPEC_CHUNKED_LOCAL = 2
 
 # Every symbol include/mvb200.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -75,6 +81,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mvb_sample": (
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _P],
+    ),
+    "mvb_build_metadata": (
+        ctypes.c_int,
+        [
+            _P, _P, _P, _P, _P, _P,  # computed, scheduled, block counts, block ids, flags, token ids
+            _I64, _I64, _I64, _I64,  # requests, tokens, block ids, sampled
+            _I64, _I64, _I64, _I64,  # request / token capacity, table width / stride
+            _I32, _I64, _I32, _I64,  # block size, null block, spec kind / param
+            _P, _P, _P, _P, _P, _P, _P, _P,  # outputs
+            _P, _P,  # status, stream
+        ],
     ),
     "mvb_attention_forward": (
         ctypes.c_int,

@@ -230,4 +230,66 @@ int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t
   return launch_sample(a);
 }
 
+int mvb_build_metadata(const int32_t* num_computed_tokens, const int32_t* num_scheduled_tokens,
+                       const int32_t* num_block_ids, const int32_t* block_ids,
+                       const uint8_t* requires_sampling, const int32_t* input_token_ids,
+                       int64_t num_requests, int64_t num_tokens, int64_t num_block_ids_total,
+                       int64_t num_sampled, int64_t request_capacity, int64_t token_capacity,
+                       int64_t table_width, int64_t table_stride, int32_t block_size,
+                       int64_t null_block_id, int32_t spec_kind, int64_t spec_param,
+                       int64_t* input_ids, int64_t* positions, int64_t* context_starts,
+                       int64_t* query_start_locations, int64_t* context_lengths,
+                       int64_t* block_table, int64_t* slot_mapping, int64_t* sampling_rows,
+                       int32_t* status, void* stream) {
+  const int64_t kLimit = (int64_t)1 << 31;
+  if (num_requests < 0 || num_tokens < 0 || num_tokens >= kLimit || num_block_ids_total < 0 ||
+      num_block_ids_total >= kLimit || num_sampled < 0 || num_sampled > num_requests ||
+      request_capacity < num_requests || token_capacity < num_tokens || table_width < 0 ||
+      block_size <= 0)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (spec_kind != MVB_SPEC_FULL && spec_kind != MVB_SPEC_SLIDING_WINDOW &&
+      spec_kind != MVB_SPEC_CHUNKED_LOCAL)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (spec_kind != MVB_SPEC_FULL && spec_param <= 0) return MVB_ERR_INVALID_ARGUMENT;
+  if (block_table && table_stride < table_width) return MVB_ERR_INVALID_ARGUMENT;
+  if (num_requests > 0 && (!num_computed_tokens || !num_scheduled_tokens || !num_block_ids))
+    return MVB_ERR_INVALID_ARGUMENT;
+  if ((num_block_ids_total > 0 && !block_ids) || (num_sampled > 0 && !requires_sampling) ||
+      (num_sampled > 0 && !sampling_rows) ||
+      (input_ids && num_tokens > 0 && !input_token_ids))
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_requests > kMaxMetadataRequests) return MVB_ERR_UNSUPPORTED_SHAPE;
+  if (token_capacity == 0 && request_capacity == 0 && !query_start_locations) return MVB_OK;
+  MetadataArgs a;
+  a.num_computed = num_computed_tokens;
+  a.num_scheduled = num_scheduled_tokens;
+  a.num_block_ids = num_block_ids;
+  a.block_ids = block_ids;
+  a.requires_sampling = requires_sampling;
+  a.input_token_ids = input_token_ids;
+  a.num_requests = num_requests;
+  a.num_tokens = num_tokens;
+  a.num_block_ids_total = num_block_ids_total;
+  a.num_sampled = num_sampled;
+  a.request_capacity = request_capacity;
+  a.token_capacity = token_capacity;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.block_size = block_size;
+  a.null_block_id = null_block_id;
+  a.spec_kind = spec_kind;
+  a.spec_param = spec_param;
+  a.input_ids = input_ids;
+  a.positions = positions;
+  a.context_starts = context_starts;
+  a.query_start_locations = query_start_locations;
+  a.context_lengths = context_lengths;
+  a.block_table = block_table;
+  a.slot_mapping = slot_mapping;
+  a.sampling_rows = sampling_rows;
+  a.status = status;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_build_metadata(a);
+}
+
 }  // extern "C"

@@ -132,6 +132,26 @@ struct SampleArgs {
 };
 int launch_sample(const SampleArgs& a);
 
+struct MetadataArgs {
+  const int32_t* num_computed;
+  const int32_t* num_scheduled;
+  const int32_t* num_block_ids;
+  const int32_t* block_ids;
+  const uint8_t* requires_sampling;
+  const int32_t* input_token_ids;
+  int64_t num_requests, num_tokens, num_block_ids_total, num_sampled;
+  int64_t request_capacity, token_capacity, table_width, table_stride;
+  int64_t block_size, null_block_id;
+  int32_t spec_kind;
+  int64_t spec_param;
+  int64_t *input_ids, *positions, *context_starts, *query_start_locations, *context_lengths;
+  int64_t *block_table, *slot_mapping, *sampling_rows;
+  int32_t* status;
+  cudaStream_t stream;
+};
+constexpr int64_t kMaxMetadataRequests = 16384;  // shared-memory offsets of every request
+int launch_build_metadata(const MetadataArgs& a);
+
 int launch_plan(const AttentionProblem& p, const WorkspaceLayout& w, int32_t group,
                 int32_t decode_ctas, int32_t prefill_block_q);
 int launch_paged_decode(const AttentionProblem& p, const WorkspaceLayout& w, int32_t grid,

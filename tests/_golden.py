@@ -98,3 +98,65 @@ def load_sampler_cases() -> dict:
         d = {k: z[k] for k in z.files}
     d["kept"] = np.unpackbits(d["kept"], axis=-1)[..., : d["logits"].shape[1]].astype(bool)
     return d
+
+
+# ---- metadata build (tests/golden/make_golden_metadata.py) ----
+
+from dataclasses import dataclass as _dataclass  # noqa: E402
+
+
+@_dataclass(frozen=True)
+class BlockIds:
+    """CacheGroupBlockTable's one field."""
+
+    block_ids: tuple
+
+
+@_dataclass(frozen=True)
+class PlanRequest:
+    """The ScheduledRequest fields (core/scheduler_output.py) a step's build reads."""
+
+    request_id: str
+    input_token_ids: tuple
+    num_computed_tokens: int
+    num_scheduled_tokens: int
+    requires_sampling: bool
+    block_tables: tuple
+
+
+@_dataclass(frozen=True)
+class Plan:
+    """SchedulerOutput's ``scheduled_requests``."""
+
+    scheduled_requests: tuple
+
+
+def metadata_manifest() -> list[dict]:
+    return json.loads((GOLDEN_DIR / "metadata_manifest.json").read_text())
+
+
+def load_metadata_case(entry: dict) -> tuple[Plan, dict]:
+    """(plan, the reference's tensors as numpy) of one golden case."""
+
+    z = np.load(GOLDEN_DIR / "metadata_cases.npz")
+    p = entry["name"] + "/"
+    ng = len(entry["group_specs"])
+    computed, scheduled = z[p + "computed"], z[p + "scheduled"]
+    sample, tokens = z[p + "sample"], z[p + "token_ids"]
+    blocks = []
+    for g in range(ng):
+        counts, ids = z[f"{p}g{g}/block_counts"], z[f"{p}g{g}/block_ids"]
+        offs = np.concatenate([[0], np.cumsum(counts)])
+        blocks.append([tuple(int(b) for b in ids[offs[i]:offs[i + 1]]) for i in range(len(counts))])
+    qsl = np.concatenate([[0], np.cumsum(scheduled)])
+    reqs = tuple(
+        PlanRequest(
+            request_id=f"r{i}", input_token_ids=tuple(int(x) for x in tokens[qsl[i]:qsl[i + 1]]),
+            num_computed_tokens=int(computed[i]), num_scheduled_tokens=int(scheduled[i]),
+            requires_sampling=bool(sample[i]),
+            block_tables=tuple(BlockIds(blocks[g][i]) for g in range(ng)),
+        )
+        for i in range(len(computed))
+    )
+    expected = {k[len(p):]: z[k] for k in z.files if k.startswith(p)}
+    return Plan(reqs), expected

@@ -140,3 +140,35 @@ def test_vocab_scale_batch() -> None:
         else:
             kept, _ = kept_and_probabilities(host[r], 0.9, int(k[r]) or None, float(p[r]))
             assert kept[got[r]]
+
+
+@pytest.mark.parametrize("case", ["large_k", "flat_top_p", "k_and_p_large"])
+def test_multi_pass_paths_keep_the_reference_set(case) -> None:
+    """Cuts whose boundary holds more than the 2048 tokens sorted in shared
+    memory: the digit-refinement passes and the draw over the whole row."""
+
+    g = torch.Generator(device=DEV).manual_seed(21)
+    vocab, rows = 50000, 64
+    scale = 0.05 if case != "large_k" else 1.0  # nearly flat: the top-p boundary bin is crowded
+    logits = (torch.randn((1, vocab), generator=g, device=DEV) * scale).expand(rows, vocab)
+    k, p = {"large_k": (3000, 1.0), "flat_top_p": (0, 0.5), "k_and_p_large": (20000, 0.7)}[case]
+    got = sample_tokens(logits, *_rows(rows, 1.0, k, p, seed=5)).cpu().numpy()
+    kept, _ = kept_and_probabilities(logits[0].float().cpu().numpy(), 1.0, k or None, p)
+    assert kept[got].all()
+    again = sample_tokens(logits, *_rows(rows, 1.0, k, p, seed=5)).cpu().numpy()
+    assert (got == again).all()
+    assert len(set(got.tolist())) > 8  # the draws spread over the kept set
+
+
+def test_exact_ties_beyond_the_shared_memory_set() -> None:
+    """10000 equal logits: top-k 100 keeps the first 100 indices; top-p 0.5
+    keeps indices 0..5000 (mass before each <= 0.5); ties in index order."""
+
+    rows, vocab = 128, 10000
+    logits = torch.zeros((rows, vocab), device=DEV)
+    got = sample_tokens(logits, *_rows(rows, 1.0, 100, 1.0, seed=3)).cpu().numpy()
+    assert got.max() < 100 and len(set(got.tolist())) > 20
+    got = sample_tokens(logits, *_rows(rows, 1.0, 0, 0.5, seed=3)).cpu().numpy()
+    assert got.max() <= 5000 and got.max() > 1000
+    got = sample_tokens(logits, *_rows(rows, 1.0, 3000, 0.1, seed=3)).cpu().numpy()
+    assert got.max() <= 300  # top-k 3000, then 10 % of its mass: indices 0..300

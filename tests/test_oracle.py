@@ -370,3 +370,97 @@ def test_sampler_oracle_reference_test_cases() -> None:
     assert kept.tolist() == [False, False, False, True, True]
     kept, _ = kept_and_probabilities(np.array([0.0, 1.0, 2.0]), 1.0, 3, 1.0)
     assert kept.all()
+
+
+# ---------------------------------------------------------------- metadata build
+from _golden import BlockIds, PlanRequest, load_metadata_case, metadata_manifest  # noqa: E402
+from oracle.metadata import PlannedRequest  # noqa: E402
+from oracle.metadata import build as build_step  # noqa: E402
+from oracle.metadata import pad as pad_step  # noqa: E402
+
+
+def _planned(plan) -> list[PlannedRequest]:
+    return [
+        PlannedRequest(q.input_token_ids, q.num_computed_tokens, q.num_scheduled_tokens, q.requires_sampling,
+                       tuple(t.block_ids for t in q.block_tables))
+        for q in plan.scheduled_requests
+    ]
+
+
+@pytest.mark.parametrize("entry", metadata_manifest(), ids=lambda e: e["name"])
+def test_metadata_oracle_matches_reference_golden(entry) -> None:
+    """Every tensor of the reference's ModelRunner._build_model_input and of
+    _CudaGraphExecution.copy_input (make_golden_metadata.py), bit-exact."""
+
+    plan, z = load_metadata_case(entry)
+    specs = [tuple(s) for s in entry["group_specs"]]
+    batch = build_step(_planned(plan), entry["block_size"], entry["null_block_id"], specs)
+    for key in ("input_ids", "positions", "query_start_locations", "context_lengths", "sampling_rows"):
+        np.testing.assert_array_equal(batch[key], z[key], err_msg=key)
+    for g, grp in enumerate(batch["groups"]):
+        for key in ("block_table", "slot_mapping", "context_starts"):
+            np.testing.assert_array_equal(grp[key], z[f"g{g}/{key}"], err_msg=f"g{g} {key}")
+    padded = pad_step(batch, entry["token_capacity"], entry["request_capacity"], entry["table_widths"][0],
+                      entry["null_block_id"])
+    for key in ("input_ids", "positions", "query_start_locations", "context_lengths"):
+        np.testing.assert_array_equal(padded[key], z["pad/" + key], err_msg="pad " + key)
+    for g, grp in enumerate(padded["groups"]):
+        for key in ("block_table", "slot_mapping", "context_starts"):
+            np.testing.assert_array_equal(grp[key], z[f"g{g}/pad/{key}"], err_msg=f"pad g{g} {key}")
+
+
+def _req(tokens, computed, sample, *tables):
+    return PlannedRequest(tuple(tokens), computed, len(tokens), sample, tuple(tuple(t) for t in tables))
+
+
+def test_metadata_oracle_reference_test_cases() -> None:
+    """Known answers of the reference's runner tests (tests/worker/
+    test_model_runner.py:213-520), restated on the oracle."""
+
+    full = [("full", 0)]
+    b = build_step([_req((10, 11, 12), 0, True, (0,))], 4, 7, full)  # :213-235
+    assert b["positions"].tolist() == [0, 1, 2] and b["query_start_locations"].tolist() == [0, 3]
+    assert b["context_lengths"].tolist() == [3] and b["sampling_rows"].tolist() == [2]
+    b = build_step([_req((12, 13), 2, False, (0,))], 4, 7, full)  # :256-268
+    assert b["positions"].tolist() == [2, 3] and b["sampling_rows"].tolist() == []
+    b = build_step([_req((20,), 4, True, (0, 1)), _req((30, 31, 32), 0, False, (2,))], 4, 7, full)  # :271-293
+    assert b["input_ids"].tolist() == [20, 30, 31, 32] and b["positions"].tolist() == [4, 0, 1, 2]
+    assert b["query_start_locations"].tolist() == [0, 1, 4] and b["context_lengths"].tolist() == [5, 3]
+    assert b["sampling_rows"].tolist() == [0]
+    b = build_step([_req((10,), 3, True, (0,)), _req((20, 21), 5, True, (0, 1))], 4, 7, full)  # :296-313
+    assert b["sampling_rows"].tolist() == [0, 2]
+    b = build_step([_req((10,), 4, False, (2, 3, 4), (7, 7, 5))], 2, 7, [("full", 0), ("sliding", 3)])  # :316-380
+    assert b["groups"][0]["context_starts"].tolist() == [0] and b["groups"][1]["context_starts"].tolist() == [2]
+    assert b["groups"][0]["block_table"].tolist() == [[2, 3, 4]]
+    assert b["groups"][1]["block_table"].tolist() == [[7, 7, 5]]
+    assert b["groups"][0]["slot_mapping"].tolist() == [8] and b["groups"][1]["slot_mapping"].tolist() == [10]
+    b = build_step([_req((10, 11), 3, False, (2, 5))], 4, 7, full)  # :383-402
+    assert b["groups"][0]["slot_mapping"].tolist() == [11, 20]
+    b = build_step([_req((10,), 4, False, (0, 3)), _req((20, 21), 1, False, (6,))], 4, 7, full)  # :405-430
+    assert b["groups"][0]["slot_mapping"].tolist() == [12, 25, 26]
+    b = build_step([_req((10,), 0, False, (2,)), _req((20,), 4, False, (3, 5, 6))], 4, 7, full)  # :455-485
+    assert b["groups"][0]["block_table"].tolist() == [[2, 7, 7], [3, 5, 6]]
+    b = build_step([], 4, 7, full)  # :508-518
+    assert b["groups"][0]["block_table"].shape == (0, 0)
+    with pytest.raises(IndexError):  # a position past the request's blocks
+        build_step([_req((10,), 4, False, (2,))], 4, 7, full)
+
+
+def test_metadata_spec_codes_and_builder_needs_cuda() -> None:
+    from micro_vllm_b200 import ChunkedLocalSpec, DeviceMetadataBuilder, FullAttentionSpec, SlidingWindowSpec
+    from micro_vllm_b200 import _lib
+    from micro_vllm_b200.metadata import spec_code
+
+    assert spec_code(FullAttentionSpec()) == (_lib.MVB_SPEC_FULL, 0)
+    assert spec_code(SlidingWindowSpec(7)) == (_lib.MVB_SPEC_SLIDING_WINDOW, 7)
+    assert spec_code(ChunkedLocalSpec(64)) == (_lib.MVB_SPEC_CHUNKED_LOCAL, 64)
+
+    class Odd:
+        def context_start(self, p):
+            return p
+
+    with pytest.raises(ValueError):
+        spec_code(Odd())
+    with pytest.raises(RuntimeError):
+        DeviceMetadataBuilder([FullAttentionSpec()], 16, 0, "cpu")
+    assert BlockIds((1,)).block_ids == (1,) and PlanRequest("a", (), 0, 0, False, ()).request_id == "a"
