@@ -45,6 +45,7 @@ namespace {
 
 constexpr int kTile = 16;
 constexpr int kStages = 3;
+constexpr int kWin = 256;  // block-table entries the producer keeps in shared memory
 constexpr int kHeadRow = kDecodeHeadDim * 2;  // bytes of one head's row
 constexpr int kWaitLimit = 1 << 22;
 
@@ -188,7 +189,7 @@ struct Slot {  // per-stage header written by the producer
 // ------------------------------------------------------------ producer
 __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
                         uint8_t* ring, Slot* slots, uint32_t full0, uint32_t empty0,
-                        int32_t stage_bytes, int32_t plane_stride, int32_t rowp) {
+                        int32_t stage_bytes, int32_t plane_stride, int32_t rowp, int64_t* win) {
   const int lane = threadIdx.x & 31;
   const int hb = p.heads_per_cta;
   const int row = lane & 15, plane = lane >> 4;
@@ -198,6 +199,7 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
   Extent e = extent_of(p, r);
   int64_t req_lo = __ldg(p.tile_prefix + r), req_hi = __ldg(p.tile_prefix + r + 1);
   const int64_t* trow = p.table + r * p.table_stride;
+  int64_t win_r = -1, win_lo = 0;  // request and first page held in win[]
   int k = 0;
   for (int64_t x = first; x < last; ++x, ++k) {
     const int64_t g = x / tiles, local = x - g * tiles;
@@ -216,8 +218,6 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
       e = extent_of(p, r);
       trow = p.table + r * p.table_stride;
     }
-    // The page lookup (a global load) goes out before the wait for a free
-    // stage, so its latency overlaps the wait.
     const int64_t tile = local - req_lo;
     const int64_t pos = e.base + tile * kTile + row;
     int64_t off, lb;
@@ -231,7 +231,21 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
     // -2: outside the visible extent; -1: outside the table.
     const bool in_extent = pos >= e.lo && pos < e.hi;
     const bool in_table = pos >= 0 && lb < p.table_width;
-    const int64_t raw_blk = in_extent && in_table ? __ldg(trow + lb) : 0;  // checked after the wait
+    // Page lookups come from a window of the request's block table that the
+    // warp loads into shared memory with coalesced loads (once per request
+    // and per 256 pages), so no tile waits on a dependent global load.
+    const bool need = in_extent && in_table;
+    if (__any_sync(0xffffffffu, need && (r != win_r || lb < win_lo || lb >= win_lo + kWin))) {
+      const int64_t lo0 = __shfl_sync(0xffffffffu, lb, 0);  // row 0 holds the tile's first page
+      for (int j = lane; j < kWin; j += 32) {
+        const int64_t q = lo0 + j;
+        win[j] = q < p.table_width ? __ldg(trow + q) : 0;
+      }
+      __syncwarp();
+      win_r = r;
+      win_lo = lo0;
+    }
+    const int64_t raw_blk = need ? win[lb - win_lo] : 0;  // checked after the wait
     const int s = k % kStages;
     if (!mbar_wait(empty0 + 8 * s, ((k / kStages) & 1) ^ 1, p.status)) {
       // A consumer stopped: let the copies already issued land before the
@@ -324,40 +338,61 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     // ---- one 16-token tile of KV head kvh ----
     const uint32_t kb = smem_u32(ring + s * stage_bytes) + w * kHeadRow;
     const uint32_t vb = kb + plane_stride;
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    // Two accumulators halve the dependent chain of the 8 k-steps.
+    float sc[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
       uint32_t a[4];
       ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, a);
-      mma16816<T>(sc, a, qb[ks][0], qb[ks][1]);
+      if (ks & 1)
+        mma16816<T>(sc2, a, qb[ks][0], qb[ks][1]);
+      else
+        mma16816<T>(sc, a, qb[ks][0], qb[ks][1]);
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[i] += sc2[i];
     const int64_t p0 = e.base + (int64_t)slot.tile * kTile + g, p1 = p0 + 8;
     const bool ok0 = (slot.row_mask >> g) & 1u, ok1 = (slot.row_mask >> (g + 8)) & 1u;
-    float corr[2], pr[4];
+    // Online softmax with a lazily moved reference: m[j] (the column's
+    // running max) moves only when a score exceeds it by more than 2^8, so
+    // most tiles need neither the column-max shuffles nor a rescale of O.
+    // O and l share the reference, so O / l is exact whatever it is, and
+    // P <= 2^8 stays well inside fp16 / bf16.
+    float sv[4], pr[4];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float s0 = (ok0 && p0 >= wlo[j] && p0 <= whi[j]) ? sc[j] * p.scale_log2 : -INFINITY;
-      const float s1 =
-          (ok1 && p1 >= wlo[j] && p1 <= whi[j]) ? sc[2 + j] * p.scale_log2 : -INFINITY;
-      float tmax = fmaxf(s0, s1);
-      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-      const float mn = fmaxf(m[j], tmax);
-      const float mu = mn == -INFINITY ? 0.f : mn;
-      corr[j] = exp2f(m[j] - mu);
-      pr[j] = exp2f(s0 - mu);
-      pr[2 + j] = exp2f(s1 - mu);
-      l[j] = l[j] * corr[j] + pr[j] + pr[2 + j];
-      m[j] = mn;
+      sv[j] = (ok0 && p0 >= wlo[j] && p0 <= whi[j]) ? sc[j] * p.scale_log2 : -INFINITY;
+      sv[2 + j] = (ok1 && p1 >= wlo[j] && p1 <= whi[j]) ? sc[2 + j] * p.scale_log2 : -INFINITY;
+    }
+    const bool jump = sv[0] > m[0] + 8.f || sv[2] > m[0] + 8.f || sv[1] > m[1] + 8.f || sv[3] > m[1] + 8.f;
+    if (__any_sync(0xffffffffu, jump)) {
+      float corr[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float tmax = fmaxf(sv[j], sv[2 + j]);
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+        const float mn = fmaxf(m[j], tmax);
+        corr[j] = exp2f(m[j] - (mn == -INFINITY ? 0.f : mn));
+        l[j] *= corr[j];
+        m[j] = mn;
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= corr[0];
+        o[mt][1] *= corr[1];
+        o[mt][2] *= corr[0];
+        o[mt][3] *= corr[1];
+      }
     }
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      o[mt][0] *= corr[0];
-      o[mt][1] *= corr[1];
-      o[mt][2] *= corr[0];
-      o[mt][3] *= corr[1];
+    for (int j = 0; j < 2; ++j) {
+      const float mu = m[j] == -INFINITY ? 0.f : m[j];
+      pr[j] = exp2f(sv[j] - mu);
+      pr[2 + j] = exp2f(sv[2 + j] - mu);
+      l[j] += pr[j] + pr[2 + j];
     }
     const uint32_t ph0 = pack2<T>(pr[0], pr[1]), ph1 = pack2<T>(pr[2], pr[3]);
     const uint32_t pb0 = movmatrix_t(ph0);
@@ -571,6 +606,7 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(8) uint64_t bars[2 * kStages];
   __shared__ Slot slots[kStages];
+  __shared__ int64_t table_win[kWin];
   const int hb = p.heads_per_cta;
   const int32_t rowp = hb * kHeadRow + 16;
   const int32_t plane_stride = kTile * rowp;
@@ -592,7 +628,8 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
   if (first >= last) return;
   const int warp = threadIdx.x >> 5;
   if (warp == hb) {
-    produce(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride, rowp);
+    produce(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride, rowp,
+            table_win);
   } else {
     consume<T>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
                plane_stride, rowp);

@@ -1,0 +1,70 @@
+"""One-copy upload of a step's host inputs.
+
+A step's inputs that live on the host (query/key/value rows and the
+attention metadata, when the caller builds them there) are packed into one
+pinned buffer, 16-byte aligned per tensor, and reach the device with a single
+``cudaMemcpyAsync``; the device tensors are views into one device buffer.
+The reference moves each metadata tensor with its own ``torch.tensor(...,
+device=...)`` (src/micro_vllm/worker/model_runner.py:751-900), one copy per
+tensor.
+"""
+
+from __future__ import annotations
+
+import torch
+
+_ALIGN = 16
+
+
+class PinnedStaging:
+    """Fixed layout for a set of named tensors (shapes and dtypes of the
+    first ``pack``); ``pack`` copies host tensors into the pinned buffer and
+    ``upload`` issues the one copy and returns device views by name."""
+
+    __slots__ = ("device", "_layout", "_host", "_dev", "_uploaded")
+
+    def __init__(self, device: torch.device | str) -> None:
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("PinnedStaging uploads to a CUDA device")
+        self._layout: dict[str, tuple[int, torch.dtype, tuple[int, ...]]] | None = None
+        self._host: torch.Tensor | None = None
+        self._dev: torch.Tensor | None = None
+        self._uploaded: torch.cuda.Event | None = None
+
+    @property
+    def nbytes(self) -> int:
+        return 0 if self._host is None else self._host.numel()
+
+    def pack(self, tensors: dict[str, torch.Tensor]) -> None:
+        if self._layout is None:
+            layout, off = {}, 0
+            for name, t in tensors.items():
+                layout[name] = (off, t.dtype, tuple(t.shape))
+                off += -(-t.numel() * t.element_size() // _ALIGN) * _ALIGN
+            self._layout = layout
+            self._host = torch.empty(off, dtype=torch.uint8).pin_memory()
+            self._dev = torch.empty(off, dtype=torch.uint8, device=self.device)
+        if self._uploaded is not None:
+            self._uploaded.synchronize()  # the last upload has left the pinned buffer
+        for name, t in tensors.items():
+            off, dtype, shape = self._layout[name]
+            if t.dtype != dtype or tuple(t.shape) != shape:
+                raise ValueError(f"{name}: {t.dtype} {tuple(t.shape)} does not match the staged layout")
+            n = t.numel() * t.element_size()
+            self._host[off:off + n].view(dtype).view(shape).copy_(t)
+
+    def upload(self) -> dict[str, torch.Tensor]:
+        assert self._layout is not None and self._host is not None and self._dev is not None
+        stream = torch.cuda.current_stream(self.device)
+        self._dev.copy_(self._host, non_blocking=True)
+        self._uploaded = torch.cuda.Event()
+        self._uploaded.record(stream)
+        out = {}
+        for name, (off, dtype, shape) in self._layout.items():
+            n = 1
+            for d in shape:
+                n *= d
+            nbytes = n * torch.empty((), dtype=dtype).element_size()
+            out[name] = self._dev[off:off + nbytes].view(dtype).view(shape)
+        return out

@@ -114,3 +114,11 @@ def test_registry_resolves_the_operator_and_rejects_unknown_names() -> None:
     assert get_attention_operator_class("b200_paged") is B200PagedAttentionOperator
     with pytest.raises(ValueError, match=r"unsupported attention operator 'unknown'.*b200_paged"):
         get_attention_operator_class("unknown")
+
+
+def test_pinned_staging_needs_cuda() -> None:
+    import pytest
+    from micro_vllm_b200.staging import PinnedStaging
+
+    with pytest.raises(RuntimeError):
+        PinnedStaging("cpu")

@@ -268,3 +268,22 @@ def test_builder_metadata_drives_the_operator() -> None:
     ref = op(q, k, v, cache2, ref_md)
     assert torch.equal(out, ref) and torch.equal(cache, cache2)
     assert builder.read_status() == 0
+
+
+def test_pinned_staging_round_trip() -> None:
+    """One pinned buffer, one copy: the device views hold the host tensors."""
+
+    from micro_vllm_b200.staging import PinnedStaging
+
+    g = torch.Generator().manual_seed(2)
+    host = {"a": torch.randn((3, 5), generator=g).half(), "b": torch.arange(7), "c": torch.randn(1, generator=g)}
+    st = PinnedStaging(DEV)
+    st.pack(host)
+    for _ in range(2):
+        d = st.upload()
+        for k, t in host.items():
+            assert torch.equal(d[k].cpu(), t) and d[k].device == DEV
+        host["b"] = host["b"] + 1
+        st.pack(host)
+    with pytest.raises(ValueError):
+        st.pack({"a": torch.zeros(2)})
