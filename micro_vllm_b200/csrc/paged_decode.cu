@@ -338,17 +338,30 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     // ---- one 16-token tile of KV head kvh ----
     const uint32_t kb = smem_u32(ring + s * stage_bytes) + w * kHeadRow;
     const uint32_t vb = kb + plane_stride;
+    // The tile's K and V fragments go to registers first, and the stage is
+    // released before any math: the producer refills it while this warp
+    // computes, so a stage is held for the 16 loads, not the whole tile.
+    uint32_t ka[8][4], va[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, ka[ks]);
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int row = (lane & 7) + (lane >> 4) * 8;
+      ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, va[mt]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);  // release: orders the loads above first
     // Two accumulators halve the dependent chain of the 8 k-steps.
     float sc[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-      uint32_t a[4];
-      ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, a);
       if (ks & 1)
-        mma16816<T>(sc2, a, qb[ks][0], qb[ks][1]);
+        mma16816<T>(sc2, ka[ks], qb[ks][0], qb[ks][1]);
       else
-        mma16816<T>(sc, a, qb[ks][0], qb[ks][1]);
+        mma16816<T>(sc, ka[ks], qb[ks][0], qb[ks][1]);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) sc[i] += sc2[i];
@@ -409,14 +422,9 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     }
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
-      const int row = (lane & 7) + (lane >> 4) * 8;
-      uint32_t a[4];
-      ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, a);
-      mma16816<T>(o[mt], a, pb0, pb1);
-      if constexpr (kSplitP) mma16816<T>(o[mt], a, pl0, pl1);
+      mma16816<T>(o[mt], va[mt], pb0, pb1);
+      if constexpr (kSplitP) mma16816<T>(o[mt], va[mt], pl0, pl1);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * s);
 
     // ---- end of this CTA's segment of the request ----
     const bool req_done = slot.tile == req_tiles - 1;
