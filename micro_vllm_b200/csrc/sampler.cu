@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
   extern __shared__ __align__(16) unsigned char sample_smem_raw[];
   SampleSmem& s = *reinterpret_cast<SampleSmem*>(sample_smem_raw);
   const int64_t row = blockIdx.x;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int esz = p.elem == MVB_DTYPE_F32 ? 4 : 2;
   RowReader rd;
   rd.ptr = p.logits + row * p.row_stride * esz;
