@@ -21,7 +21,7 @@ class PinnedStaging:
     first ``pack``); ``pack`` copies host tensors into the pinned buffer and
     ``upload`` issues the one copy and returns device views by name."""
 
-    __slots__ = ("device", "_layout", "_host", "_dev", "_uploaded")
+    __slots__ = ("device", "_layout", "_host", "_dev", "_uploaded", "_views")
 
     def __init__(self, device: torch.device | str) -> None:
         self.device = torch.device(device)
@@ -31,6 +31,7 @@ class PinnedStaging:
         self._host: torch.Tensor | None = None
         self._dev: torch.Tensor | None = None
         self._uploaded: torch.cuda.Event | None = None
+        self._views: dict[str, torch.Tensor] | None = None
 
     @property
     def nbytes(self) -> int:
@@ -55,16 +56,21 @@ class PinnedStaging:
             self._host[off:off + n].view(dtype).view(shape).copy_(t)
 
     def upload(self) -> dict[str, torch.Tensor]:
+        """One host-to-device copy; the returned device views are the same
+        tensors every call (the layout is fixed), so they may be held."""
+
         assert self._layout is not None and self._host is not None and self._dev is not None
         stream = torch.cuda.current_stream(self.device)
         self._dev.copy_(self._host, non_blocking=True)
         self._uploaded = torch.cuda.Event()
         self._uploaded.record(stream)
-        out = {}
-        for name, (off, dtype, shape) in self._layout.items():
-            n = 1
-            for d in shape:
-                n *= d
-            nbytes = n * torch.empty((), dtype=dtype).element_size()
-            out[name] = self._dev[off:off + nbytes].view(dtype).view(shape)
-        return out
+        if self._views is None:
+            views = {}
+            for name, (off, dtype, shape) in self._layout.items():
+                n = 1
+                for d in shape:
+                    n *= d
+                nbytes = n * torch.empty((), dtype=dtype).element_size()
+                views[name] = self._dev[off:off + nbytes].view(dtype).view(shape)
+            self._views = views
+        return dict(self._views)
