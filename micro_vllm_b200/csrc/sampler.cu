@@ -59,6 +59,7 @@ constexpr int kTile = kThreads * kVec;  // tokens per tile
 constexpr int kBins = 2048;             // 11-bit key digits
 constexpr int kMassBins = 4096;         // top-p value bins
 constexpr int kCap = 2048;              // boundary candidates sorted in shared memory
+constexpr int kSeg = 256;               // each warp's segment of the candidate buffer
 constexpr uint32_t kFull = 0xffffffffu;
 
 // Digit levels of the 32-bit key: bits 31..21, 20..10, 9..0.
@@ -85,11 +86,13 @@ struct SampleParams {
 struct SampleSmem {
   uint32_t hist[kMassBins];
   unsigned long long mass[kMassBins];
-  unsigned long long cand[kCap];    // (key << 32) | ~index: descending = key desc, index asc
-  unsigned long long cand_e[kCap];  // mass of each candidate (top-p)
+  // (key << 32) | ~index: descending = key desc, index asc.  Warp w appends
+  // to [w * kSeg, (w + 1) * kSeg); collect() compacts to [0, count).
+  unsigned long long cand[kWarps * kSeg];
   unsigned long long red64[kWarps];
   float redf[kWarps];
   uint32_t ncand;
+  uint32_t wcnt[kWarps];
   uint32_t sel_bin, sel_rank, sel_cnt, sel_none, sel_above_cnt, sel_lo;
   unsigned long long sel_above;
   long long found;
@@ -488,9 +491,8 @@ __device__ __forceinline__ void pick_range(SampleSmem& s, unsigned long long tp)
   }
 }
 
-// Bitonic sort of s.cand[0, n) (n a power of two, <= kCap) descending,
-// carrying s.cand_e along when with_mass.
-__device__ __forceinline__ void sort_candidates(SampleSmem& s, int n, bool with_mass) {
+// Bitonic sort of s.cand[0, n) (n a power of two, <= kCap) descending.
+__device__ __forceinline__ void sort_candidates(SampleSmem& s, int n) {
   for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < n; i += kThreads) {
@@ -501,11 +503,6 @@ __device__ __forceinline__ void sort_candidates(SampleSmem& s, int n, bool with_
           if (desc ? (a < b) : (a > b)) {
             s.cand[i] = b;
             s.cand[ixj] = a;
-            if (with_mass) {
-              const unsigned long long t = s.cand_e[i];
-              s.cand_e[i] = s.cand_e[ixj];
-              s.cand_e[ixj] = t;
-            }
           }
         }
       }
@@ -641,39 +638,51 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
   // set that starts at the largest token: its first n entries are the
   // kept-by-k tokens (all of them without top-k), top-p is a scan of their
   // masses and the draw a scan of the kept masses (in sorted order).
-  // Candidate slots come from one shared counter; collect() sorts the
-  // gathered candidates and returns their number (at most kCap).
+  // Candidates go to per-warp segments (one counter per warp, so appends
+  // from different warps never contend on an address); collect() compacts
+  // them through s.mass and sorts the keys.  A candidate's mass is not
+  // stored: it is a function of its logit, which its key holds, so cmass(i)
+  // recomputes it after the sort.  collect() returns the number of
+  // candidates, or -1 when a warp overflowed its segment or they exceed kCap.
+  auto seg_reset = [&]() {
+    if (tid < kWarps) s.wcnt[tid] = 0;
+    __syncthreads();
+  };
+  auto push = [&](uint32_t key, int64_t i) {
+    const uint32_t slot = atomicAdd(&s.wcnt[warp], 1u);
+    if (slot < (uint32_t)kSeg) s.cand[warp * kSeg + slot] = cand_of(key, i);
+  };
   auto collect = [&]() -> int {
     __syncthreads();
-    const int c = (int)min(s.ncand, (uint32_t)kCap);
-    const int n2 = pow2_at_least(c);
-    for (int i = c + tid; i < n2; i += kThreads) {
-      s.cand[i] = 0ull;
-      s.cand_e[i] = 0ull;
+    uint32_t total = 0, off = 0;
+    bool over = false;
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t c = s.wcnt[w];
+      over |= c > (uint32_t)kSeg;
+      if (w < warp) off += c;
+      total += c;
     }
+    if (over || total > (uint32_t)kCap) return -1;
+    const uint32_t mine = s.wcnt[warp];
+    for (uint32_t i = tid & 31; i < mine; i += 32) s.mass[off + i] = s.cand[warp * kSeg + i];
     __syncthreads();
-    sort_candidates(s, n2, true);
+    const int c = (int)total, n2 = pow2_at_least(c);
+    for (int i = tid; i < n2; i += kThreads) s.cand[i] = i < c ? s.mass[i] : 0ull;  // pads sort last
+    __syncthreads();
+    sort_candidates(s, n2);
     return c;
   };
-  auto push = [&](uint32_t key, int64_t i, unsigned long long m) {
-    const uint32_t slot = atomicAdd(&s.ncand, 1u);
-    if (slot < (uint32_t)kCap) {
-      s.cand[slot] = cand_of(key, i);
-      s.cand_e[slot] = m;
-    }
+  auto cmass = [&](int i) -> unsigned long long {
+    return mass_of(key_value((uint32_t)(s.cand[i] >> 32)), c1, c2);
   };
   auto gather = [&](auto want, bool positive_only) -> int {
-    if (tid == 0) s.ncand = 0;
-    __syncthreads();
+    seg_reset();
     for_each_tile(rd, tid, [&](const int64_t i0, const float (&v)[kVec], const int n) {
 #pragma unroll
       for (int j = 0; j < kVec; ++j) {
         const float x = v[j];
         const uint32_t key = order_key(x);
-        if (j < n && want(x, key, i0 + j)) {
-          const unsigned long long m = mass_of(x, c1, c2);
-          if (!positive_only || m > 0) push(key, i0 + j, m);
-        }
+        if (j < n && want(x, key, i0 + j) && (!positive_only || mass_of(x, c1, c2) > 0)) push(key, i0 + j);
       }
     });
     return collect();
@@ -684,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
-      if (i < n) mine += s.cand_e[i];
+      if (i < n) mine += cmass(i);
     }
     unsigned long long tot;
     const unsigned long long exc = block_excl_scan(mine, s, &tot);
@@ -703,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
             atomicMin(&s.found, (long long)i);
             break;
           }
-          acc += s.cand_e[i];
+          acc += cmass(i);
         }
       }
       __syncthreads();
@@ -713,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
-      if (i < keep) kmine += s.cand_e[i];
+      if (i < keep) kmine += cmass(i);
     }
     unsigned long long kept_total;
     unsigned long long before = block_excl_scan(kmine, s, &kept_total);
@@ -724,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
       if (i < keep) {
-        const unsigned long long m = s.cand_e[i];
+        const unsigned long long m = cmass(i);
         if (m > 0 && before <= target && target < before + m) p.out[row] = cand_index(s.cand[i]);
         before += m;
       }
@@ -739,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
-      if (i < c) mine += s.cand_e[i];
+      if (i < c) mine += cmass(i);
     }
     unsigned long long tot;
     const unsigned long long exc = block_excl_scan(mine, s, &tot);
@@ -754,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
           atomicMin(&s.found, (long long)i);
           break;
         }
-        acc += s.cand_e[i];
+        acc += cmass(i);
       }
     }
     __syncthreads();
@@ -831,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
       const int n2 = pow2_at_least(c);
       for (int i = c + tid; i < n2; i += kThreads) s.cand[i] = 0ull;  // sorts last
       __syncthreads();
-      sort_candidates(s, n2, false);
+      sort_candidates(s, n2);
       const unsigned long long e = s.cand[rank - 1];
       k_key = (uint32_t)(e >> 32);
       k_last = cand_index(e);
@@ -923,8 +932,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
       if (rcnt <= (uint32_t)kCap) {
         // One pass: the exact mass above the range (per thread) and the
         // range's tokens into shared memory.
-        if (tid == 0) s.ncand = 0;
-        __syncthreads();
+        seg_reset();
         unsigned long long above_mine = 0;
         for_each_tile(rd, tid, [&](const int64_t i0, const float (&v)[kVec], const int n) {
 #pragma unroll
@@ -936,8 +944,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
             if (vbin > b_hi) {
               above_mine += mass_of(x, c1, c2);
             } else if (vbin >= b_lo) {
-              const unsigned long long m = mass_of(x, c1, c2);
-              if (m > 0) push(key, i0 + j, m);
+              if (mass_of(x, c1, c2) > 0) push(key, i0 + j);
             }
           }
         });
@@ -953,7 +960,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
 #pragma unroll
           for (int q = 0; q < kPer; ++q) {
             const int i = tid * kPer + q;
-            if (i < cut) smem_add64(&s.mass[(cand_index(s.cand[i]) & (kTile - 1)) / kVec], (uint32_t)s.cand_e[i]);
+            if (i < cut) smem_add64(&s.mass[(cand_index(s.cand[i]) & (kTile - 1)) / kVec], (uint32_t)cmass(i));
           }
           __syncthreads();
           my_kept = above_mine + s.mass[tid];
@@ -963,7 +970,8 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
       }
       if (!cut_done) {
         // A crowded value bin: search by key digits, refining until the
-        // boundary holds at most kCap tokens.
+        // boundary holds at most one warp segment of tokens (so no warp
+        // overflows its segment when they are gathered).
         for (int b = tid; b < kBins; b += kThreads) {
           s.hist[b] = 0;
           s.mass[b] = 0ull;
@@ -986,7 +994,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
         uint32_t prefix = s.sel_bin << digit_shift(0), cnt = s.sel_cnt;
         unsigned long long above = s.sel_above;
         int levels = 1;
-        while (cnt > (uint32_t)kCap && levels < 3) {
+        while (cnt > (uint32_t)kSeg && levels < 3) {
           const int nb = digit_bins(levels), shift = digit_shift(levels);
           const uint32_t done = done_mask(levels);
           __syncthreads();
@@ -1014,7 +1022,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
           cnt = s.sel_cnt;
           ++levels;
         }
-        if (cnt > (uint32_t)kCap) {  // more than kCap kept tokens share the exact key
+        if (cnt > (uint32_t)kSeg) {  // more than kSeg kept tokens share the exact key
           const unsigned long long q = mass_of(key_value(prefix), c1, c2);
           unsigned long long j = q > 0 ? (tp - above) / q + 1 : (unsigned long long)cnt;
           if (j > cnt) j = cnt;
