@@ -79,14 +79,15 @@ def test_prologue_matches_reference_golden(name: str) -> None:
     np.testing.assert_array_equal(got_cache[1], exp_cache[1])
 
 
-def _random_case(dtype: torch.dtype, tokens: int, hq: int, hkv: int, seed: int):
+def _random_case(dtype: torch.dtype, tokens: int, hq: int, hkv: int, seed: int, lead: int = 0):
     g = torch.Generator().manual_seed(seed)
     d, bs, nb = 128, 16, 64
-    # q, k, v as views of one fused projection output (strided rows).
-    fused = (torch.randn((tokens, (hq + 2 * hkv) * d), generator=g) * 2.0).to(dtype).to(DEV)
-    q = fused[:, : hq * d].view(tokens, hq, d)
-    k = fused[:, hq * d : (hq + hkv) * d].view(tokens, hkv, d)
-    v = fused[:, (hq + hkv) * d :].view(tokens, hkv, d)
+    # q, k, v as views of one fused projection output (strided rows); `lead`
+    # extra elements in front of each row leave rows only 8-byte aligned.
+    fused = (torch.randn((tokens, lead + (hq + 2 * hkv) * d), generator=g) * 2.0).to(dtype).to(DEV)
+    q = fused[:, lead : lead + hq * d].unflatten(1, (hq, d))
+    k = fused[:, lead + hq * d : lead + (hq + hkv) * d].unflatten(1, (hkv, d))
+    v = fused[:, lead + (hq + hkv) * d :].unflatten(1, (hkv, d))
     positions = torch.randint(0, 100_000, (tokens,), generator=g).to(DEV)
     slots = torch.randperm(nb * bs, generator=g)[:tokens].to(DEV)
     slots[5] = -1
@@ -107,9 +108,14 @@ def _oracle(q, k, v, positions, slots, q_w, k_w, eps, inv_freq, cache, dt):
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
-@pytest.mark.parametrize("hq,hkv", [(16, 8), (32, 8), (8, 8), (14, 2)])
-def test_prologue_matches_oracle_on_strided_views(dt: str, hq: int, hkv: int) -> None:
-    q, k, v, positions, slots, q_w, k_w, cache, bs = _random_case(TORCH_DTYPE[dt], 300, hq, hkv, hq + hkv)
+@pytest.mark.parametrize("hq,hkv,lead", [(16, 8, 0), (32, 8, 0), (8, 8, 0), (14, 2, 0), (15, 3, 0),
+                                         (16, 8, 4), (15, 3, 4)])
+def test_prologue_matches_oracle_on_strided_views(dt: str, hq: int, hkv: int, lead: int) -> None:
+    """lead 0: 16-byte rows (two rows per warp instruction; 15/3 puts a query
+    and a key row, then a key and a value row, in one instruction); lead 4:
+    8-byte rows (one row per warp instruction)."""
+
+    q, k, v, positions, slots, q_w, k_w, cache, bs = _random_case(TORCH_DTYPE[dt], 300, hq, hkv, hq + hkv, lead)
     inv = rotary_inverse_frequencies(128, 1e6, DEV)
     exp_q, exp_cache = _oracle(q, k, v, positions, slots, q_w, k_w, 1e-6, inv, cache, dt)
     q_out = qk_norm_rope_and_write(q, k, v, positions, q_w, k_w, 1e-6, inv, cache, _metadata(slots, bs))
