@@ -122,6 +122,11 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t total;
   __shared__ int32_t bucket[kOrderBuckets];
+  // A copy of tile_prefix for the decode CTAs' searches below (batches of up
+  // to kSmemPrefix requests), so they read shared rather than global memory.
+  constexpr int kSmemPrefix = 2048;
+  __shared__ int64_t prefix_sh[kSmemPrefix + 1];
+  const bool prefix_in_smem = p.num_requests <= kSmemPrefix;
 
   // Per-request decode tile counts and prefill query-tile counts, and their
   // exclusive prefix sums.
@@ -137,7 +142,10 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
         units = (p.qsl[r + 1] - p.qsl[r] + p.prefill_block_q - 1) / p.prefill_block_q;
     }
     const int64_t incl = block_inclusive_scan(tiles, warp_tot, &total);
-    if (r < p.num_requests) p.tile_prefix[r] = running + incl - tiles;
+    if (r < p.num_requests) {
+      p.tile_prefix[r] = running + incl - tiles;
+      if (prefix_in_smem) prefix_sh[r] = running + incl - tiles;
+    }
     running += total;
     __syncthreads();
     const int64_t incl_u = block_inclusive_scan(units, warp_tot, &total);
@@ -151,6 +159,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
   }
   if (threadIdx.x == 0) {
     p.tile_prefix[p.num_requests] = running;
+    if (prefix_in_smem) prefix_sh[p.num_requests] = running;
     p.prefill_prefix[p.num_requests] = running_units;
     p.ctrl[kCtrlTiles] = running;
     p.ctrl[kCtrlPrefillUnits] = running_units;
@@ -205,7 +214,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
       int64_t lo = 0, hi = p.num_requests;  // largest r with tile_prefix[r] <= local
       while (lo < hi) {
         const int64_t mid = (lo + hi) >> 1;
-        if (p.tile_prefix[mid] <= local)
+        if ((prefix_in_smem ? prefix_sh[mid] : p.tile_prefix[mid]) <= local)
           lo = mid + 1;
         else
           hi = mid;
