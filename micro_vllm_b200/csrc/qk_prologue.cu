@@ -16,9 +16,10 @@
 //
 // One warp per token: it evaluates the token's rotation angles once, then
 // walks its rows — the Hq query heads, the Hkv key heads, the Hkv value
-// heads — in batches of 8 loaded together.  A lane owns 4 consecutive
-// elements of the 128-element row, so rotate_half's partner of lane l is
-// lane l ^ 16.
+// heads — in batches of 8 loaded together.  A lane owns columns 2l, 2l+1 and
+// 2l+64, 2l+65 of the 128-element row, so rotate_half's partner of every
+// column is in the same lane; the 8 rows of a batch share one transposed
+// warp reduction of their statistics.
 // Roofline: HBM; bytes per token = (Hq + 2 Hkv) * D * elsize read +
 // (Hq + 2 Hkv) * D * elsize written.
 #include <cuda_bf16.h>
@@ -56,51 +57,74 @@ struct PrologueParams {
   int32_t* status;
 };
 
+// Two adjacent 16-bit elements as one 32-bit word, and the paired ops on them.
 template <typename T>
-__device__ __forceinline__ float to_f(T v);
+struct Pair;
 template <>
-__device__ __forceinline__ float to_f<__half>(__half v) {
-  return __half2float(v);
-}
+struct Pair<__half> {
+  static __device__ __forceinline__ float2 to_f2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  // Correctly rounded product of two 16-bit values (exact in fp32, one rounding).
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    const __half2 h = __hmul2_rn(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
 template <>
-__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
-  return __bfloat162float(v);
-}
-template <typename T>
-__device__ __forceinline__ T from_f(float v);
-template <>
-__device__ __forceinline__ __half from_f<__half>(float v) {
-  return __float2half_rn(v);
-}
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
-  return __float2bfloat16_rn(v);
-}
-// Round through the model dtype.
-template <typename T>
-__device__ __forceinline__ float rnd(float v) {
-  return to_f<T>(from_f<T>(v));
+struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 to_f2(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  }
+  static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    const __nv_bfloat162 h = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                        *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+};
+
+// Sum over the warp of 8 per-lane values s[0..7], transposed: lane l ends
+// with the total of value (l >> 2) & 7.  9 shuffles for 8 rows instead of 40.
+__device__ __forceinline__ float reduce8_transposed(const float (&s)[8], int lane) {
+  float t[4], u[2];
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = b16 ? s[i + 4] : s[i], send = b16 ? s[i] : s[i + 4];
+    t[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b8 ? t[i + 2] : t[i], send = b8 ? t[i] : t[i + 2];
+    u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float v = (b4 ? u[1] : u[0]) + __shfl_xor_sync(0xffffffffu, b4 ? u[0] : u[1], 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
 }
 
-// 4 consecutive 16-bit elements as one 8-byte word.
-template <typename T>
-__device__ __forceinline__ void unpack4(uint2 w, float (&x)[4]) {
-  const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = to_f<T>(e[i]);
-}
-template <typename T>
-__device__ __forceinline__ uint2 pack4(const float (&x)[4]) {
-  uint2 w;
-  T* e = reinterpret_cast<T*>(&w);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) e[i] = from_f<T>(x[i]);
-  return w;
+// Row r of token t: the query heads, then the key heads, then the value heads.
+__device__ __forceinline__ const char* row_of(const PrologueParams& p, int64_t t, int r) {
+  if (r < p.num_q_heads) return p.q + (t * p.q_st + (int64_t)r * p.q_sh) * 2;
+  r -= p.num_q_heads;
+  if (r < p.num_kv_heads) return p.k + (t * p.k_st + (int64_t)r * p.k_sh) * 2;
+  r -= p.num_kv_heads;
+  return p.v + (t * p.v_st + (int64_t)r * p.v_sh) * 2;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(32 * kPrologueWarps)
     qk_prologue_kernel(const PrologueParams p) {
+  using P = Pair<T>;
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kPrologueWarps + (threadIdx.x >> 5);
   if (t >= p.num_tokens) return;
@@ -112,80 +136,84 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
   if (slot >= p.num_slots && lane == 0 && p.status != nullptr)
     atomicOr(p.status, MVB_STATUS_SLOT_OUT_OF_RANGE);
 
-  // Rotation of this lane's columns 4*lane..4*lane+3, once per token:
-  // column c and c + 64 share frequency c mod 64 (angles = cat(freqs, freqs)).
-  float cs[4], sn[4], qw[4], kw[4];
+  // Lane l owns columns 2l, 2l+1 (word l of the row) and 2l+64, 2l+65 (word
+  // l+32): rotate_half pairs column c with c + 64, so both partners sit in
+  // one lane, and c and c + 64 share frequency c (angles = cat(freqs, freqs)).
+  float cs[2], sn[2];
   {
     const float pf = (float)__ldg(p.pos + t);  // positions.to(float32)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float ang = __fmul_rn(pf, __ldg(p.inv_freq + ((4 * lane + i) & 63)));
+    for (int i = 0; i < 2; ++i) {
+      const float ang = __fmul_rn(pf, __ldg(p.inv_freq + 2 * lane + i));
       sincosf(ang, &sn[i], &cs[i]);
     }
-    unpack4<T>(__ldg(reinterpret_cast<const uint2*>(p.q_w) + lane), qw);
-    unpack4<T>(__ldg(reinterpret_cast<const uint2*>(p.k_w) + lane), kw);
   }
+  const uint32_t* qw = reinterpret_cast<const uint32_t*>(p.q_w);
+  const uint32_t* kw = reinterpret_cast<const uint32_t*>(p.k_w);
+  const uint32_t qw_lo = __ldg(qw + lane), qw_hi = __ldg(qw + 32 + lane);
+  const uint32_t kw_lo = __ldg(kw + lane), kw_hi = __ldg(kw + 32 + lane);
 
   for (int r0 = 0; r0 < rows; r0 += kRowsPerWarp) {
     const int nr = min(kRowsPerWarp, rows - r0);
     // A batch of rows in flight at once.
-    uint2 raw[kRowsPerWarp];
+    uint32_t lo[kRowsPerWarp], hi[kRowsPerWarp];
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i) {
-      raw[i] = make_uint2(0, 0);
+      lo[i] = hi[i] = 0;
       if (i < nr) {
-        const int r = r0 + i;
-        const char* base;
-        if (r < p.num_q_heads)
-          base = p.q + (t * p.q_st + (int64_t)r * p.q_sh) * 2;
-        else if (r < qk_rows)
-          base = p.k + (t * p.k_st + (int64_t)(r - p.num_q_heads) * p.k_sh) * 2;
-        else
-          base = p.v + (t * p.v_st + (int64_t)(r - qk_rows) * p.v_sh) * 2;
-        raw[i] = __ldg(reinterpret_cast<const uint2*>(base) + lane);
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(row_of(p, t, r0 + i));
+        lo[i] = __ldg(row + lane);
+        hi[i] = __ldg(row + 32 + lane);
       }
     }
+    // RMSNorm statistics of the batch's rows: per-lane sums of squares
+    // (fp32), then one transposed warp reduction and one reciprocal root per
+    // lane for all 8 rows; row i's factor is then read from lane 4i.
+    float ss[kRowsPerWarp];
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i) {
+      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
+      ss[i] = (a.x * a.x + a.y * a.y) + (b.x * b.x + b.y * b.y);
+    }
+    const float tot = reduce8_transposed(ss, lane);
+    const float inv_lane = 1.0f / sqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / kPrologueDim), p.eps));
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const float inv_rms = __shfl_sync(0xffffffffu, inv_lane, 4 * i);
       if (i >= nr) break;
       const int r = r0 + i;
       if (r >= qk_rows) {  // value row: straight into plane 1
         if (write) {
-          char* dst = p.cache + ((p.num_slots + slot) * p.num_kv_heads + (r - qk_rows)) *
-                                    (int64_t)kPrologueDim * 2;
-          reinterpret_cast<uint2*>(dst)[lane] = raw[i];
+          uint32_t* dst = reinterpret_cast<uint32_t*>(
+              p.cache + ((p.num_slots + slot) * p.num_kv_heads + (r - qk_rows)) * (int64_t)kPrologueDim * 2);
+          dst[lane] = lo[i];
+          dst[32 + lane] = hi[i];
         }
         continue;
       }
       const bool is_q = r < p.num_q_heads;
-      float x[4];
-      unpack4<T>(raw[i], x);
-      // RMSNorm: mean of squares over the row, fp32.
-      float ss = x[0] * x[0];
-      ss = __fadd_rn(ss, __fmul_rn(x[1], x[1]));
-      ss = __fadd_rn(ss, __fmul_rn(x[2], x[2]));
-      ss = __fadd_rn(ss, __fmul_rn(x[3], x[3]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      const float inv_rms = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / kPrologueDim), p.eps));
-      float y[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        y[e] = rnd<T>(__fmul_rn(is_q ? qw[e] : kw[e], rnd<T>(__fmul_rn(x[e], inv_rms))));
-      // rotate_half: the first half takes -x[c + 64], the second x[c - 64].
-      float out[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float partner = __shfl_xor_sync(0xffffffffu, y[e], 16);
-        const float rot = lane < 16 ? -partner : partner;
-        out[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(rot, sn[e]));
-      }
-      const uint2 w = pack4<T>(out);
-      if (is_q) {
-        reinterpret_cast<uint2*>(p.q_out + ((t * p.num_q_heads + r) * (int64_t)kPrologueDim) * 2)[lane] = w;
-      } else if (write) {
-        char* dst = p.cache + (slot * p.num_kv_heads + (r - p.num_q_heads)) * (int64_t)kPrologueDim * 2;
-        reinterpret_cast<uint2*>(dst)[lane] = w;
+      // The normalised value rounded to the model dtype, times the weight
+      // (one correctly rounded 16-bit product, as the fp32 product rounded).
+      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
+      const float2 ya = P::to_f2(P::mul(P::from_f2(__fmul_rn(a.x, inv_rms), __fmul_rn(a.y, inv_rms)),
+                                        is_q ? qw_lo : kw_lo));
+      const float2 yb = P::to_f2(P::mul(P::from_f2(__fmul_rn(b.x, inv_rms), __fmul_rn(b.y, inv_rms)),
+                                        is_q ? qw_hi : kw_hi));
+      // x * cos + rotate_half(x) * sin, products and sum rounded separately:
+      // column c < 64 takes -x[c + 64], column c + 64 takes x[c].
+      const uint32_t out_lo = P::from_f2(__fadd_rn(__fmul_rn(ya.x, cs[0]), __fmul_rn(-yb.x, sn[0])),
+                                         __fadd_rn(__fmul_rn(ya.y, cs[1]), __fmul_rn(-yb.y, sn[1])));
+      const uint32_t out_hi = P::from_f2(__fadd_rn(__fmul_rn(yb.x, cs[0]), __fmul_rn(ya.x, sn[0])),
+                                         __fadd_rn(__fmul_rn(yb.y, cs[1]), __fmul_rn(ya.y, sn[1])));
+      uint32_t* dst = nullptr;
+      if (is_q)
+        dst = reinterpret_cast<uint32_t*>(p.q_out + ((t * p.num_q_heads + r) * (int64_t)kPrologueDim) * 2);
+      else if (write)
+        dst = reinterpret_cast<uint32_t*>(p.cache + (slot * p.num_kv_heads + (r - p.num_q_heads)) *
+                                                        (int64_t)kPrologueDim * 2);
+      if (dst != nullptr) {
+        dst[lane] = out_lo;
+        dst[32 + lane] = out_hi;
       }
     }
   }
