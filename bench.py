@@ -364,6 +364,9 @@ def run_ours(args) -> None:
     clocks.start()
     t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    # A ~100 us spin keeps the GPU busy while the host enqueues the start
+    # event and the first step, so the timed region holds device work only.
+    torch.cuda._sleep(200_000)
     t_start.record(stream)
     for _ in range(args.steps):
         step()
@@ -374,6 +377,7 @@ def run_ours(args) -> None:
     # ---- decode kernel alone (plan + decode launches) ----
     barrier()
     a_start, a_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(200_000)
     a_start.record(stream)
     for _ in range(args.steps):
         attention_only()
@@ -556,6 +560,7 @@ def run_mixed(args) -> None:
         for _ in range(max(args.warmup, 3)):
             fn()
         torch.cuda.synchronize(dev)
+        torch.cuda._sleep(200_000)  # GPU busy while the host enqueues the first launch
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         for _ in range(steps):
@@ -750,6 +755,7 @@ def run_sample(args) -> None:
     total = 0.0
     for _ in range(args.steps):
         flush.max()
+        torch.cuda._sleep(200_000)  # GPU busy while the host enqueues the event and the launch
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         step()
