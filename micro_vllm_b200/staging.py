@@ -7,6 +7,10 @@ pinned buffer, 16-byte aligned per tensor, and reach the device with a single
 The reference moves each metadata tensor with its own ``torch.tensor(...,
 device=...)`` (src/micro_vllm/worker/model_runner.py:751-900), one copy per
 tensor.
+
+``UploadPipeline`` keeps two such buffers and a copy stream, so that the
+upload of the next step's inputs and the read-back of the previous step's
+result overlap the current step's kernels.
 """
 
 from __future__ import annotations
@@ -56,8 +60,9 @@ class PinnedStaging:
             self._host[off:off + n].view(dtype).view(shape).copy_(t)
 
     def upload(self) -> dict[str, torch.Tensor]:
-        """One host-to-device copy; the returned device views are the same
-        tensors every call (the layout is fixed), so they may be held."""
+        """One host-to-device copy on the current stream; the returned device
+        views are the same tensors every call (the layout is fixed), so they
+        may be held."""
 
         assert self._layout is not None and self._host is not None and self._dev is not None
         stream = torch.cuda.current_stream(self.device)
@@ -74,3 +79,59 @@ class PinnedStaging:
                 views[name] = self._dev[off:off + nbytes].view(dtype).view(shape)
             self._views = views
         return dict(self._views)
+
+
+class UploadPipeline:
+    """Double-buffered uploads and read-backs on their own streams.
+
+    ``slot(i)`` is step i's ``PinnedStaging`` (two, used in turn: pack each
+    once, or again before its step).  ``upload(i)`` copies slot i % 2 to the
+    device on the upload stream, once the kernels that last read that slot's
+    device buffer (step i - 2) have finished, and makes the current stream
+    wait for that copy alone; it returns the device views.  ``download(i,
+    result, host)`` reads the step's result back on the read-back stream once
+    the current stream has produced it.  ``drain()`` makes the current stream
+    wait for every copy issued so far.  Step i's kernels then overlap step
+    i + 1's upload and step i - 1's read-back.
+    """
+
+    __slots__ = ("device", "_slots", "_h2d", "_d2h", "_released")
+
+    def __init__(self, device: torch.device | str) -> None:
+        self.device = torch.device(device)
+        self._slots = (PinnedStaging(self.device), PinnedStaging(self.device))
+        self._h2d = torch.cuda.Stream(self.device)
+        self._d2h = torch.cuda.Stream(self.device)
+        self._released: list[torch.cuda.Event | None] = [None, None]
+
+    def slot(self, i: int) -> PinnedStaging:
+        return self._slots[i % 2]
+
+    def upload(self, i: int) -> dict[str, torch.Tensor]:
+        compute = torch.cuda.current_stream(self.device)
+        released = self._released[i % 2]
+        if released is not None:
+            self._h2d.wait_event(released)
+        else:  # first use: after everything the caller queued so far
+            self._h2d.wait_stream(compute)
+        with torch.cuda.stream(self._h2d):
+            views = self._slots[i % 2].upload()
+            copied = torch.cuda.Event()
+            copied.record(self._h2d)
+        compute.wait_event(copied)
+        return views
+
+    def download(self, i: int, result: torch.Tensor, host: torch.Tensor) -> None:
+        compute = torch.cuda.current_stream(self.device)
+        done = torch.cuda.Event()
+        done.record(compute)  # this step's kernels, the last readers of its device buffer
+        self._released[i % 2] = done
+        self._d2h.wait_event(done)
+        with torch.cuda.stream(self._d2h):
+            host.copy_(result, non_blocking=True)
+        result.record_stream(self._d2h)
+
+    def drain(self) -> None:
+        compute = torch.cuda.current_stream(self.device)
+        compute.wait_stream(self._h2d)
+        compute.wait_stream(self._d2h)

@@ -287,3 +287,27 @@ def test_pinned_staging_round_trip() -> None:
         st.pack(host)
     with pytest.raises(ValueError):
         st.pack({"a": torch.zeros(2)})
+
+
+def test_upload_pipeline_steps_in_order() -> None:
+    """Double-buffered uploads and read-backs: every step sees its own inputs
+    and every host result is its own step's, with slow kernels in between
+    (a slot is not overwritten while its step still reads it)."""
+
+    from micro_vllm_b200.staging import UploadPipeline
+
+    steps, n = 6, 4096
+    g = torch.Generator().manual_seed(5)
+    inputs = [{"x": torch.randn(n, generator=g), "y": torch.full((n,), float(i))} for i in range(steps)]
+    outs = [torch.empty(n).pin_memory() for _ in range(steps)]
+    pipe = UploadPipeline(DEV)
+    for i in range(steps):
+        pipe.slot(i).pack(inputs[i])  # waits for the slot's previous upload on the host
+        d = pipe.upload(i)
+        torch.cuda._sleep(2_000_000)  # a long step: the next upload runs beside it
+        result = d["x"] * 2 + d["y"]
+        pipe.download(i, result, outs[i])
+    pipe.drain()
+    torch.cuda.synchronize(DEV)
+    for i in range(steps):
+        assert torch.equal(outs[i], inputs[i]["x"] * 2 + inputs[i]["y"])
