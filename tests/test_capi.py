@@ -118,7 +118,9 @@ def test_registry_resolves_the_operator_and_rejects_unknown_names() -> None:
 
 def test_pinned_staging_needs_cuda() -> None:
     import pytest
-    from micro_vllm_b200.staging import PinnedStaging
+    from micro_vllm_b200.staging import PinnedStaging, UploadPipeline
 
     with pytest.raises(RuntimeError):
         PinnedStaging("cpu")
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        UploadPipeline("cpu")
