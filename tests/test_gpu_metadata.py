@@ -311,3 +311,38 @@ def test_upload_pipeline_steps_in_order() -> None:
     torch.cuda.synchronize(DEV)
     for i in range(steps):
         assert torch.equal(outs[i], inputs[i]["x"] * 2 + inputs[i]["y"])
+
+
+def test_upload_pipeline_drives_the_operator() -> None:
+    """The benchmark's end-to-end path: a decode step's q/k/v and metadata
+    from pinned host memory through the pipeline give the same output, bit
+    for bit, as the operator on device inputs."""
+
+    from micro_vllm_b200 import B200PagedAttentionOperator
+    from micro_vllm_b200.staging import UploadPipeline
+    from micro_vllm_b200.workloads import paged_batch
+
+    ctx = [37, 300, 1, 129, 64]
+    batch = paged_batch(context_lengths=ctx, query_lengths=[1] * len(ctx), num_q_heads=16, num_kv_heads=8,
+                        head_dim=128, block_size=16, num_blocks=256, dtype=torch.float16, device=DEV, seed=3)
+    op = B200PagedAttentionOperator()
+    md = batch.metadata
+    ref = op(batch.query, batch.key, batch.value, batch.cache, md).cpu()
+    host = {"q": batch.query.cpu(), "k": batch.key.cpu(), "v": batch.value.cpu(),
+            "pos": md.query_positions.cpu(), "start": md.query_context_start_positions.cpu(),
+            "qsl": md.query_start_locations.cpu(), "ctx": md.context_lengths.cpu(),
+            "table": md.block_table.cpu(), "slots": md.slot_mapping.cpu()}
+    pipe = UploadPipeline(DEV)
+    pipe.slot(0).pack(host)
+    pipe.slot(1).pack(host)
+    outs = [torch.empty(ref.shape, dtype=ref.dtype).pin_memory() for _ in range(4)]
+    for i in range(4):
+        d = pipe.upload(i)
+        emd = AttentionMetadata(query_positions=d["pos"], query_context_start_positions=d["start"],
+                                query_start_locations=d["qsl"], context_lengths=d["ctx"],
+                                block_table=d["table"], slot_mapping=d["slots"], block_size=16)
+        pipe.download(i, op(d["q"], d["k"], d["v"], batch.cache, emd), outs[i])
+    pipe.drain()
+    torch.cuda.synchronize(DEV)
+    for o in outs:
+        assert torch.equal(o, ref)
