@@ -107,9 +107,17 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
-    ap.add_argument("--workload", choices=("decode", "mixed", "llama8b", "prologue", "sample", "metadata"),
+    ap.add_argument("--workload",
+                    choices=("decode", "mixed", "llama8b", "prologue", "sample", "metadata", "engine"),
                     default="decode",
-                    help="decode: BASELINE config 2 (headline); mixed: config 3 (prefill + decode)")
+                    help="decode: BASELINE config 2 (headline, with the config-5 engine object); "
+                         "mixed: config 3 (prefill + decode); engine: config 5 alone")
+    ap.add_argument("--no-engine", action="store_true",
+                    help="decode workload without the config-5 engine measurement")
+    ap.add_argument("--engine-requests", type=int, default=512)
+    ap.add_argument("--engine-max-tokens", type=int, default=256)
+    ap.add_argument("--no-engine-baselines", action="store_true",
+                    help="skip the reference engine configurations timed beside ours at N=1")
     ap.add_argument("--pool-gb", type=float, default=None,
                     help="pool size in GB instead of 80%% of HBM (small cases for ncu captures)")
     return ap.parse_args()
@@ -276,8 +284,50 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- ranks
+def init_ranks():
+    """(world size, rank, this rank's device); one NCCL process group for the
+    job (torchrun's environment), created once, with a short timeout so
+    ranks waiting on a failed one end with an error."""
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, dev
+
+
+def finish_ranks() -> None:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _reduce(value: float, op: str, dev) -> float:
+    """MAX / MIN / SUM of a host number over the ranks (identity at N=1)."""
+
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
+    return float(t.item())
+
+
 # ---------------------------------------------------------------- GPU
-def run_ours(args) -> None:
+def run_ours(args) -> dict:
     import torch
     import torch.distributed as dist
 
@@ -285,15 +335,8 @@ def run_ours(args) -> None:
     from micro_vllm_b200 import _lib
     from micro_vllm_b200.workloads import paged_batch, pool_blocks_for_fraction
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    world, rank, dev = init_ranks()
+    local = dev.index
     shape = DecodeShape(args)
     hq = shape.hq
     dtype = torch.float16 if shape.dtype == "fp16" else torch.bfloat16
@@ -518,11 +561,171 @@ def run_ours(args) -> None:
         line["config"]["shard_imbalance"] = max(s.work for s in shards) / (sum(s.work for s in shards) / world)
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, elsize, args.cpu_sample_seconds)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
+
+
+# ---------------------------------------------------------------- config 5
+ENGINE_CHECKPOINT = "/tmp/mvb200_random_qwen3_0_6b_seed0"
+
+
+def _engine_config(path, operator: str, graphs: bool, args):
+    import torch
+    from micro_vllm.config import CacheConfig, LLMConfig, ModelConfig, SchedulerConfig
+    from micro_vllm_b200.integration import register
+
+    register()  # b200_paged may take CUDA graphs: ModelConfig checks at construction
+    return LLMConfig(
+        model_config=ModelConfig(model=str(path), attention_operator=operator, enable_cuda_graph=graphs,
+                                 device="cuda", dtype=torch.float16),
+        scheduler_config=SchedulerConfig(max_num_batched_tokens=8192, max_num_seqs=512, max_model_len=1280),
+        cache_config=CacheConfig(block_size=16, gpu_memory_utilization=0.9),
+    )
+
+
+def _engine_once(name: str, operator: str, graphs: bool, options, requests, args, dev) -> dict:
+    """Initialise one worker, warm it with a short run, then time the
+    requests to completion through a fresh Engine."""
+
+    import gc
+
+    import torch
+    from micro_vllm_b200.engine import build_worker, fresh_engine, run_engine
+
+    # Every rank takes the same collectives whatever fails: one MIN after
+    # the set-up (also the start barrier of the timed run), none inside it.
+    t0 = time.perf_counter()
+    worker = config = None
+    error = None
+    try:
+        config = _engine_config(ENGINE_CHECKPOINT, operator, graphs, args)
+        worker = build_worker(config, options)
+        warm = [type(r)(r.request_id, r.prompt_token_ids, 4) for r in requests[:8]]
+        run_engine(fresh_engine(worker, config), warm, dev)
+    except Exception as exc:
+        error = f"{type(exc).__name__}: {exc}"
+    init_s = time.perf_counter() - t0
+    try:
+        if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
+            raise RuntimeError(error or "another rank failed to set up its engine")
+        run = run_engine(fresh_engine(worker, config), requests, dev)
+    finally:
+        if worker is not None:
+            worker.shutdown()
+        del worker
+        gc.collect()
+        torch.cuda.empty_cache()
+    return {"name": name, "seconds": run.seconds, "wall_seconds": run.wall_seconds, "steps": run.steps,
+            "output_tokens": run.output_tokens, "prompt_tokens": run.prompt_tokens, "init_seconds": init_s,
+            "outputs": run.outputs}
+
+
+def engine_measure(args) -> dict:
+    """output tokens/s of the reference's own engine
+    (scheduler, KV block manager, engine loop, Qwen3 model) with the
+    ``b200_paged`` operator and ``B200ModelRunner``, on a random-init
+    Qwen3-0.6B in fp16.  The 512 requests are partitioned over the ranks
+    longest-first on prompt + max_tokens (one engine replica per GPU, no
+    collective on the data path): strong scaling of a fixed job.  Each rank
+    times its Engine.step loop with CUDA events; the job time is the max over
+    ranks.  At N=1 the reference's fastest engine configuration
+    (``triton_paged`` with CUDA graphs, its stock runner) runs the same job."""
+
+    import traceback
+
+    world, rank, dev = init_ranks()
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    error = None
+    try:
+        from micro_vllm_b200.engine import QWEN3_0_6B, RunnerOptions, engine_requests, write_random_checkpoint
+        from micro_vllm_b200.partition import partition_sequences
+
+        if rank == 0 and not (Path(ENGINE_CHECKPOINT) / "config.json").exists():
+            write_random_checkpoint(ENGINE_CHECKPOINT + ".tmp", QWEN3_0_6B, seed=0)
+            os.replace(ENGINE_CHECKPOINT + ".tmp", ENGINE_CHECKPOINT)
+    except Exception as exc:  # the reference is not installed, or the checkpoint failed
+        error = f"{type(exc).__name__}: {exc}"
+    if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
+        return {"unavailable": error or "another rank could not prepare the engine"}
+
+    requests = engine_requests(args.engine_requests, max_tokens=args.engine_max_tokens, seed=0)
+    shards = partition_sequences([len(r.prompt_token_ids) + r.max_tokens for r in requests], world)
+    mine = [requests[i] for i in shards[rank].indices]
+    result = None
+    try:
+        result = _engine_once("b200", "b200_paged", True, RunnerOptions(), mine, args, dev)
+    except Exception:
+        error = traceback.format_exc(limit=3).strip().splitlines()[-1]
+    if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
+        return {"unavailable": error or "another rank failed in the engine run"}
+    seconds = _reduce(result["seconds"], "max", dev)
+    wall = _reduce(result["wall_seconds"], "max", dev)
+    tokens = _reduce(float(result["output_tokens"]), "sum", dev)
+    steps = _reduce(float(result["steps"]), "max", dev)
+    out = {
+        "metric": "engine output tokens/s (BASELINE config 5)",
+        "value": tokens / seconds,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "scaling": "strong",
+        "seconds": seconds,
+        "wall_seconds": wall,
+        "output_tokens": int(tokens),
+        "max_steps_over_ranks": int(steps),
+        "config": {
+            "model": "Qwen3-0.6B shape (28 layers, hidden 1024, 16/8 heads, head_dim 128, MLP 3072, vocab 151936), "
+                     "random init N(0, 0.02) seed 0, fp16",
+            "requests": len(requests),
+            "prompt_len": "U[128,1024] token ids U[1,151935]",
+            "max_tokens": args.engine_max_tokens,
+            "sampling": "greedy, ignore_eos",
+            "max_num_batched_tokens": 8192, "max_num_seqs": 512, "max_model_len": 1280, "block_size": 16,
+            "cuda_graphs": True,
+            "attention_operator": "b200_paged",
+            "runner": "B200ModelRunner: device metadata build, batched device sampler, fused Qwen3 prologue",
+            "partition": f"LPT on prompt + max_tokens over {world} engine replicas, no data-path collective",
+            "requests_per_rank_max": max(len(sh.indices) for sh in shards),
+        },
+        "timing": "CUDA events around each rank's Engine.step loop (synchronised at both ends), max over ranks; "
+                  "wall_seconds is the host clock around the same loop",
+    }
+    if world == 1 and not args.no_engine_baselines:
+        try:
+            ref = _engine_once("triton_paged", "triton_paged", True, None, mine, args, dev)
+            out["reference_engine"] = {
+                "value": ref["output_tokens"] / ref["seconds"], "unit": "tokens/s", "seconds": ref["seconds"],
+                "steps": ref["steps"],
+                "what": "the reference's stock ModelRunner with attention_operator='triton_paged' and CUDA "
+                        "graphs (its fastest engine configuration), same model, requests and limits",
+            }
+        except Exception:
+            out["reference_engine"] = {"unavailable": traceback.format_exc(limit=3).strip().splitlines()[-1]}
+    return out
+
+
+def run_engine_workload(args) -> None:
+    """``--workload engine``: the config-5 measurement as its own line."""
+
+    world, rank, dev = init_ranks()
+    eng = engine_measure(args)
+    finish_ranks()
+    if rank != 0:
+        return
+    line = {
+        "metric": "engine_output_tokens_per_s",
+        "value": eng.get("value"),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE config 5: engine, random-init Qwen3-0.6B, 512 requests"},
+        "engine": eng,
+    }
+    print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- config 3
@@ -1019,8 +1222,21 @@ def main() -> None:
         run_sample(args)
     elif args.workload == "metadata":
         run_metadata(args)
+    elif args.workload == "engine":
+        run_engine_workload(args)
     else:
-        run_ours(args)
+        line = run_ours(args)
+        if not args.no_engine and args.workload == "decode":
+            import gc
+
+            import torch
+
+            gc.collect()
+            torch.cuda.empty_cache()  # the decode pool goes back before the engine sizes its cache
+            line["engine"] = engine_measure(args)
+        finish_ranks()
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,381 @@
+"""The reference's engine with the B200 pieces plugged in where they fit.
+
+Nothing of the reference is edited: ``register()`` makes ``"b200_paged"`` a
+selectable operator, and ``B200ModelRunner`` derives from the reference's
+``ModelRunner`` (src/micro_vllm/worker/model_runner.py:125-900), replacing
+three host-side stages of its step with this package's kernels:
+
+* ``_build_model_input`` and, under a CUDA graph, ``_CudaGraphExecution.copy_input``
+  (model_runner.py:724-900, :78-122): the step's positions, token ids,
+  query start locations, context lengths, padded block tables, slot
+  mappings, visibility starts and sampling rows come from one pinned upload
+  and one ``mvb_build_metadata`` launch per cache group
+  (``DeviceMetadataBuilder``), written straight into the captured graph's
+  fixed buffers with ``copy_input``'s padding;
+* ``Sampler`` (sampling/sampler.py:14-61, one ``.item()`` per row): every
+  row in one ``mvb_sample`` launch and one host read (``B200Sampler``);
+* in Qwen3 layers, ``q_norm``, ``k_norm``, the rotary embedding and the
+  operator's KV write (models/qwen.py:89-98) become one
+  ``mvb_qk_norm_rope_and_cache`` launch, followed by attention over the cache
+  (``B200PagedAttentionOperator.attend``).
+
+The scheduler, KV block manager, request state, engine loop, model layers
+other than attention and the GEMMs are the reference's, unchanged.
+``B200Worker`` is the reference ``Worker`` around a ``B200ModelRunner``
+(``build_worker``); ``fresh_engine`` assembles
+``Engine(Scheduler, SingleProcessExecutor(worker))`` as ``LLM.__init__`` does
+(llm.py:54-77).
+
+This module imports micro_vllm; import it only where the reference is
+installed.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import time
+import types
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Sequence
+
+import torch
+
+from micro_vllm.config import LLMConfig
+from micro_vllm.core.kv_cache_manager import KVCacheManager
+from micro_vllm.core.scheduler import Scheduler
+from micro_vllm.engine.engine import Engine
+from micro_vllm.executor.single_process import SingleProcessExecutor
+from micro_vllm.sampling.params import SamplingParams
+from micro_vllm.worker.model_runner import ModelRunner, _CudaGraphExecution
+from micro_vllm.worker.worker import Worker
+
+from micro_vllm_b200.integration import register
+from micro_vllm_b200.metadata import DeviceMetadataBuilder
+from micro_vllm_b200.operators import B200PagedAttentionOperator
+from micro_vllm_b200.prologue import Qwen3AttentionPrologue
+from micro_vllm_b200.sampling import B200Sampler
+
+
+@dataclass(frozen=True, slots=True)
+class RunnerOptions:
+    """Which reference stages ``B200ModelRunner`` replaces."""
+
+    device_metadata: bool = True
+    device_sampler: bool = True
+    fused_prologue: bool = True
+
+
+class B200ModelRunner(ModelRunner):
+    """``ModelRunner`` with the device metadata build, the batched sampler and
+    the fused Qwen3 prologue (see the module docstring)."""
+
+    def __init__(self, config: LLMConfig, options: RunnerOptions = RunnerOptions()) -> None:
+        super().__init__(config)
+        self._options = options
+        self._eager_builders: dict[int, DeviceMetadataBuilder] = {}
+        self._graph_builders: dict[int, DeviceMetadataBuilder] = {}
+        if options.device_sampler:
+            self._sampler = B200Sampler()
+
+    # -- model -------------------------------------------------------------
+    def initialize_model(self) -> None:
+        super().initialize_model()
+        if self._options.fused_prologue:
+            self._install_prologue()
+
+    def _b200_operators(self) -> list[B200PagedAttentionOperator]:
+        seen: dict[int, B200PagedAttentionOperator] = {}
+        for attention in self._model.layer_attentions:
+            if isinstance(attention.operator, B200PagedAttentionOperator):
+                seen.setdefault(id(attention.operator), attention.operator)
+        return list(seen.values())
+
+    def _install_prologue(self) -> None:
+        """Route every Qwen3 attention module whose operator is ``b200_paged``
+        through the fused prologue (fp16 / bf16 only)."""
+
+        head_dim = self._config.model_config.values.get("head_dim")
+        if self._dtype not in (torch.float16, torch.bfloat16) or head_dim != 128:
+            return
+        try:
+            from micro_vllm.models.qwen import Qwen3Attention
+        except ImportError:
+            return
+        for module in self._model.modules():
+            if not isinstance(module, Qwen3Attention):
+                continue
+            if not isinstance(module.attention.operator, B200PagedAttentionOperator):
+                continue
+            module._b200_prologue = Qwen3AttentionPrologue.from_modules(
+                module.q_norm, module.k_norm, module.rotary_embedding)
+            module.forward = types.MethodType(_qwen3_attention_forward, module)
+
+    # -- step inputs ---------------------------------------------------------
+    def _layer_specs(self) -> list:
+        return [attention.spec for attention in self._model.layer_attentions]
+
+    def _build_model_input(self, plan, null_block_id: int):
+        if not self._options.device_metadata:
+            return super()._build_model_input(plan, null_block_id)
+        builder = self._eager_builders.get(null_block_id)
+        if builder is None:
+            builder = DeviceMetadataBuilder(
+                self._layer_specs(), self._block_size, null_block_id, self._device)
+            self._eager_builders[null_block_id] = builder
+        return builder.build(plan)
+
+    def _make_cuda_graph_input(self, num_tokens: int, num_requests: int, null_block_id: int):
+        if not self._options.device_metadata:
+            return super()._make_cuda_graph_input(num_tokens, num_requests, null_block_id)
+        width = math.ceil(self._config.scheduler_config.max_model_len / self._block_size)
+        builder = DeviceMetadataBuilder(
+            self._layer_specs(), self._block_size, null_block_id, self._device,
+            token_capacity=num_tokens, request_capacity=num_requests, table_width=width)
+        self._graph_builders[num_tokens] = builder
+        # The captured forward reads these buffers: start from copy_input's
+        # padding of an empty batch (model_runner.py:78-122).
+        return builder.build_empty()
+
+    def _capture_cuda_graphs(self, layout, kv_cache_buffers):
+        scheduler = self._config.scheduler_config
+        values = self._config.model_config.values
+        hq = int(values["num_attention_heads"])
+        hkv = int(values.get("num_key_value_heads", hq))
+        head_dim = int(values.get("head_dim") or int(values["hidden_size"]) // hq)
+        for operator in self._b200_operators():
+            operator.reserve(
+                self._device, max_num_tokens=scheduler.max_num_batched_tokens,
+                max_num_requests=scheduler.max_num_seqs, num_q_heads=hq,
+                num_kv_heads=hkv, head_dim=head_dim)
+        return super()._capture_cuda_graphs(layout, kv_cache_buffers)
+
+    # -- one step ----------------------------------------------------------------
+    def execute(self, plan, /):
+        if not self._options.device_metadata:
+            return super().execute(plan)
+        model = self._model
+        kv_cache_buffers = self._kv_cache_buffers
+        if model is None or kv_cache_buffers is None:
+            raise RuntimeError("model runner is not initialized")
+        null_block_id = self._kv_cache_layout.num_blocks - 1
+        num_tokens = sum(request.num_scheduled_tokens for request in plan.scheduled_requests)
+        graph_size = self._graph_size(num_tokens)
+        layer_kv_caches = self._bind_layer_kv_caches(kv_cache_buffers)
+        with torch.inference_mode():
+            if graph_size is None:
+                model_input = self._build_model_input(plan, null_block_id)
+                hidden_states = self._forward_model(model_input, layer_kv_caches)
+            else:
+                model_input = self._graph_builders[graph_size].build(plan)
+                execution: _CudaGraphExecution = self._cuda_graph_executions[graph_size]
+                execution.graph.replay()
+                hidden_states = execution.hidden_states
+            logits = self._compute_logits(hidden_states, model_input.sampling_row_indices)
+        sampled = tuple(request for request in plan.scheduled_requests if request.requires_sampling)
+        return self._sampler(
+            logits,
+            tuple(request.request_id for request in sampled),
+            tuple(request.sampling_params for request in sampled),
+            tuple(request.sample_index for request in sampled),
+        )
+
+    def _graph_size(self, num_tokens: int) -> int | None:
+        if num_tokens == 0:
+            return None
+        for size in sorted(self._cuda_graph_executions):
+            if num_tokens <= size:
+                return size
+        return None
+
+
+def _qwen3_attention_forward(self, hidden_states, positions, layer_kv_cache, metadata):
+    """``Qwen3Attention.forward`` (models/qwen.py:69-98) with q/k norm, RoPE and
+    the KV write fused into one launch, then attention over the cache."""
+
+    query = self.q_proj(hidden_states).view(-1, self.num_attention_heads, self.head_dim)
+    key = self.k_proj(hidden_states).view(-1, self.num_key_value_heads, self.head_dim)
+    value = self.v_proj(hidden_states).view(-1, self.num_key_value_heads, self.head_dim)
+    query = self._b200_prologue(positions, query, key, value, layer_kv_cache, metadata)
+    attention_output = self.attention.operator.attend(query, layer_kv_cache, metadata)
+    return self.o_proj(attention_output.flatten(start_dim=1))
+
+
+class B200Worker(Worker):
+    """The reference ``Worker`` (worker/worker.py:10-54) around a ``B200ModelRunner``."""
+
+    __slots__ = ()
+
+    def __init__(self, config: LLMConfig, options: RunnerOptions = RunnerOptions()) -> None:
+        runner = B200ModelRunner(config, options)
+        runner.initialize_model()
+        runner.initialize_kv_cache()
+        self._config = config
+        self._model_runner = runner
+
+
+def build_worker(config: LLMConfig, options: RunnerOptions | None = RunnerOptions()) -> Worker:
+    """A worker for ``config``: ``B200Worker`` when the operator is
+    ``b200_paged`` and ``options`` is given, else the reference's ``Worker``."""
+
+    register()
+    if options is not None and config.model_config.attention_operator == "b200_paged":
+        return B200Worker(config, options)
+    return Worker(config)
+
+
+def fresh_engine(worker: Worker, config: LLMConfig) -> Engine:
+    """A new ``Engine`` (fresh Scheduler and KVCacheManager) over an initialised
+    worker, as the reference's engine benchmark builds one per repetition
+    (benchmarks/benchmark_engine.py:146-153)."""
+
+    scheduler = Scheduler(config, KVCacheManager(config, worker.kv_cache_layout))
+    return Engine(scheduler, SingleProcessExecutor(worker))
+
+
+# -- the engine workload ---------------------------------------
+
+QWEN3_0_6B = {
+    "architectures": ["Qwen3ForCausalLM"],
+    "model_type": "qwen3",
+    "vocab_size": 151936,
+    "hidden_size": 1024,
+    "intermediate_size": 3072,
+    "num_hidden_layers": 28,
+    "num_attention_heads": 16,
+    "num_key_value_heads": 8,
+    "head_dim": 128,
+    "max_position_embeddings": 40960,
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1000000.0,
+    "hidden_act": "silu",
+    "tie_word_embeddings": True,
+    "attention_bias": False,
+    "attention_dropout": 0.0,
+    "use_sliding_window": False,
+    "torch_dtype": "float16",
+}
+
+
+def qwen3_tensor_shapes(values: dict) -> dict[str, tuple[int, ...]]:
+    """Checkpoint tensor names and shapes of a dense Qwen3 model, in the
+    Hugging Face naming the reference loader maps (models/qwen.py:248-262)."""
+
+    h = values["hidden_size"]
+    i = values["intermediate_size"]
+    hq, hkv, d = values["num_attention_heads"], values["num_key_value_heads"], values["head_dim"]
+    shapes = {"model.embed_tokens.weight": (values["vocab_size"], h), "model.norm.weight": (h,)}
+    if not values.get("tie_word_embeddings", False):
+        shapes["lm_head.weight"] = (values["vocab_size"], h)
+    for layer in range(values["num_hidden_layers"]):
+        p = f"model.layers.{layer}."
+        shapes.update({
+            p + "self_attn.q_proj.weight": (hq * d, h),
+            p + "self_attn.k_proj.weight": (hkv * d, h),
+            p + "self_attn.v_proj.weight": (hkv * d, h),
+            p + "self_attn.o_proj.weight": (h, hq * d),
+            p + "self_attn.q_norm.weight": (d,),
+            p + "self_attn.k_norm.weight": (d,),
+            p + "mlp.gate_proj.weight": (i, h),
+            p + "mlp.up_proj.weight": (i, h),
+            p + "mlp.down_proj.weight": (h, i),
+            p + "input_layernorm.weight": (h,),
+            p + "post_attention_layernorm.weight": (h,),
+        })
+    return shapes
+
+
+def write_random_checkpoint(path: str | Path, values: dict = QWEN3_0_6B, *, seed: int = 0,
+                            dtype: torch.dtype = torch.float16, std: float = 0.02) -> Path:
+    """A random-init checkpoint directory (``config.json`` + ``model.safetensors``)
+    the reference loader reads: matrices N(0, std) (the Hugging Face
+    initializer range), norm weights 1, drawn from one seeded CPU generator
+    in name order, so the same seed gives the same model anywhere."""
+
+    from safetensors.torch import save_file
+
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    gen = torch.Generator().manual_seed(seed)
+    tensors = {}
+    for name, shape in sorted(qwen3_tensor_shapes(values).items()):
+        if name.endswith("norm.weight"):
+            tensors[name] = torch.ones(shape, dtype=dtype)
+        else:
+            tensors[name] = (torch.randn(shape, generator=gen) * std).to(dtype)
+    save_file(tensors, str(path / "model.safetensors"))
+    (path / "config.json").write_text(json.dumps(values, indent=1, sort_keys=True))
+    return path
+
+
+@dataclass(frozen=True, slots=True)
+class EngineRequest:
+    request_id: str
+    prompt_token_ids: tuple[int, ...]
+    max_tokens: int
+
+
+def engine_requests(num_requests: int = 512, *, prompt_range: tuple[int, int] = (128, 1024),
+                    max_tokens: int = 256, vocab_size: int = 151936, seed: int = 0) -> list[EngineRequest]:
+    """Seeded synthetic requests: prompt lengths U[lo, hi], token ids U[1, vocab-1]."""
+
+    gen = torch.Generator().manual_seed(seed)
+    lo, hi = prompt_range
+    lengths = torch.randint(lo, hi + 1, (num_requests,), generator=gen).tolist()
+    out = []
+    for index, length in enumerate(lengths):
+        ids = torch.randint(1, vocab_size, (length,), generator=gen).tolist()
+        out.append(EngineRequest(f"request-{index}", tuple(ids), max_tokens))
+    return out
+
+
+@dataclass(frozen=True, slots=True)
+class EngineRun:
+    """One drive of the engine to completion."""
+
+    seconds: float  # CUDA events around the loop
+    wall_seconds: float  # host clock around the same loop
+    steps: int
+    output_tokens: int
+    prompt_tokens: int
+    outputs: dict[str, tuple[int, ...]]
+
+
+def run_engine(engine: Engine, requests: Sequence[EngineRequest], device: torch.device,
+               *, max_steps: int | None = None) -> EngineRun:
+    """Add every request (greedy, ``ignore_eos``), then call ``Engine.step`` until
+    none is unfinished; the time covers the step loop only, bracketed by
+    CUDA events on the current stream with a device synchronisation at
+    each end (the method of benchmarks/benchmark_engine.py:177-200, with the
+    whole loop timed once instead of per step)."""
+
+    for request in requests:
+        engine.add_request(
+            request.request_id, list(request.prompt_token_ids),
+            SamplingParams(max_tokens=request.max_tokens, ignore_eos=True, temperature=0.0, seed=0),
+        )
+    limit = max_steps if max_steps is not None else 10 * sum(
+        len(r.prompt_token_ids) + r.max_tokens for r in requests)
+    outputs: dict[str, tuple[int, ...]] = {}
+    stream = torch.cuda.current_stream(device)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter()
+    start.record(stream)
+    steps = 0
+    while engine.has_unfinished_requests():
+        if steps >= limit:
+            raise RuntimeError(f"engine did not finish within {limit} steps")
+        for output in engine.step():
+            outputs[output.request_id] = output.output_token_ids
+        steps += 1
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - wall
+    return EngineRun(
+        seconds=start.elapsed_time(stop) / 1e3, wall_seconds=wall, steps=steps,
+        output_tokens=sum(len(v) for v in outputs.values()),
+        prompt_tokens=sum(len(r.prompt_token_ids) for r in requests),
+        outputs=outputs,
+    )

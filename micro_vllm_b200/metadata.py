@@ -147,6 +147,40 @@ class DeviceMetadataBuilder:
 
         return self.launch(self.stage(plan))
 
+    def build_empty(self) -> StepInput:
+        """The fixed buffers holding a batch of no requests, padded as
+        ``copy_input`` pads (model_runner.py:78-122): zero token ids,
+        positions, context lengths and visibility starts, query start
+        locations 0, null-block tables, slots -1.  This is the state a graph
+        is captured on (``_make_cuda_graph_input``, model_runner.py:387-463)."""
+
+        if self._fixed is None:
+            raise ValueError("build_empty needs a builder with capacities")
+        out = self._fixed
+        for name in ("input_ids", "positions", "qsl", "ctx"):
+            out[name].zero_()
+        for starts, slots, table in out["groups"]:
+            starts.zero_()
+            slots.fill_(-1)
+            table.fill_(self.null_block_id)
+        return StepInput(
+            input_ids=out["input_ids"],
+            positions=out["positions"],
+            layer_attention_metadata=tuple(self._group_metadata(out)[g] for g in self.group_of_layer),
+            request_ids=tuple(f"__cuda_graph__-{i}" for i in range(self.request_capacity)),
+            sampling_row_indices=out["rows"][:0],
+        )
+
+    def _group_metadata(self, out: dict) -> list[AttentionMetadata]:
+        return [
+            AttentionMetadata(
+                query_positions=out["positions"], query_context_start_positions=starts,
+                query_start_locations=out["qsl"], context_lengths=out["ctx"], block_table=table,
+                slot_mapping=slots, block_size=self.block_size,
+            )
+            for starts, slots, table in out["groups"]
+        ]
+
     def stage(self, plan, /) -> "StagedPlan":
         """Pack the plan into pinned memory and start its upload (one copy).
 
@@ -237,14 +271,7 @@ class DeviceMetadataBuilder:
                 self.status.data_ptr(), stream,
             )
             _lib.check(rc, "b200 metadata build")
-        group_md = [
-            AttentionMetadata(
-                query_positions=out["positions"], query_context_start_positions=starts,
-                query_start_locations=out["qsl"], context_lengths=out["ctx"], block_table=table,
-                slot_mapping=slots, block_size=self.block_size,
-            )
-            for starts, slots, table in out["groups"]
-        ]
+        group_md = self._group_metadata(out)
         return StepInput(
             input_ids=out["input_ids"],
             positions=out["positions"],

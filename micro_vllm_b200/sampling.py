@@ -16,6 +16,7 @@ the token torch's generator would give.
 from __future__ import annotations
 
 import secrets
+import sys
 from dataclasses import dataclass
 
 import torch
@@ -98,7 +99,7 @@ class B200Sampler:
     def __call__(self, logits, request_ids, sampling_params, sample_indices, /) -> SamplerOutput:
         rows = len(request_ids)
         if rows == 0:
-            return SamplerOutput()
+            return _output_types()[0]()
         dev = logits.device
         temperature = torch.tensor([float(p.temperature) for p in sampling_params], dtype=torch.float32)
         top_k = torch.tensor([0 if p.top_k is None else int(p.top_k) for p in sampling_params],
@@ -111,4 +112,17 @@ class B200Sampler:
         index = torch.tensor([int(i) for i in sample_indices], dtype=torch.int64)
         packed = [t.to(dev, non_blocking=True) for t in (temperature, top_k, top_p, seed, index)]
         tokens = sample_tokens(logits, *packed).cpu()  # the one host read of the step
-        return SamplerOutput(tuple(SampledToken(r, int(t)) for r, t in zip(request_ids, tokens)))
+        output_type, token_type = _output_types()
+        return output_type(tuple(token_type(r, int(t)) for r, t in zip(request_ids, tokens.tolist())))
+
+
+def _output_types() -> tuple[type, type]:
+    """The reference's ``ModelRunnerOutput`` / ``SampledToken``
+    (executor/interface.py:9-24) when micro_vllm is loaded in this process
+    (its scheduler reads them), else this module's mirrors.  micro_vllm is
+    not imported here: importing it loads transformers."""
+
+    interface = sys.modules.get("micro_vllm.executor.interface")
+    if interface is not None:
+        return interface.ModelRunnerOutput, interface.SampledToken
+    return SamplerOutput, SampledToken

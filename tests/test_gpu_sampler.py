@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from _golden import SAMPLER_TIE_ROW, load_sampler_cases
-from micro_vllm_b200.sampling import B200Sampler, SampledToken, SamplerOutput, sample_tokens
+from micro_vllm_b200.sampling import B200Sampler, sample_tokens
 from oracle.sampler import greedy, kept_and_probabilities
 
 pytestmark = pytest.mark.gpu
@@ -101,11 +101,16 @@ def test_sampler_interface_mirrors_the_reference() -> None:
         def __init__(self, temperature=0.0, top_k=None, top_p=1.0, seed=None):
             self.temperature, self.top_k, self.top_p, self.seed = temperature, top_k, top_p, seed
 
+    from micro_vllm_b200.sampling import _output_types
+
+    # The reference's own ModelRunnerOutput when micro_vllm is loaded in this
+    # process (its scheduler consumes it), else this package's mirror.
+    output_type, token_type = _output_types()
     s = B200Sampler()
     logits = torch.tensor([[0.0, 1.0, 3.0], [4.0, 2.0, 1.0], [0.0, 5.0, 1.0]], device=DEV)
     out = s(logits, ("third", "first", "second"), (Params(),) * 3, (0, 0, 0))
-    assert out == SamplerOutput((SampledToken("third", 2), SampledToken("first", 0), SampledToken("second", 1)))
-    assert s(torch.empty((0, 4), device=DEV), (), (), ()) == SamplerOutput()
+    assert out == output_type((token_type("third", 2), token_type("first", 0), token_type("second", 1)))
+    assert s(torch.empty((0, 4), device=DEV), (), (), ()) == output_type()
     tie = torch.tensor([[1.0, 3.0, 3.0, 2.0]], device=DEV)
     assert s(tie, ("r",), (Params(),), (0,)).sampled_tokens[0].token_id == 1
     topk = torch.tensor([[0.0, 1.0, 2.0, 3.0, 4.0]], device=DEV)
