@@ -112,6 +112,8 @@ def parse_args() -> argparse.Namespace:
                     default="decode",
                     help="decode: BASELINE config 2 (headline, with the config-5 engine object); "
                          "mixed: config 3 (prefill + decode); engine: config 5 alone")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip the reference's Triton kernel timed beside ours on the decode batch")
     ap.add_argument("--no-engine", action="store_true",
                     help="decode workload without the config-5 engine measurement")
     ap.add_argument("--engine-requests", type=int, default=512)
@@ -327,6 +329,63 @@ def _reduce(value: float, op: str, dev) -> float:
 
 
 # ---------------------------------------------------------------- GPU
+def triton_comparator(batch, ours, dev, samples: int = 10, launches: int = 5) -> dict:
+    """The reference's own GPU kernel on the same batch and pool:
+    ``triton_paged_attention`` (src/micro_vllm/attention/operators/triton_paged.py:328-389
+    in the reference project: its one-launch KV write, then one program per
+    block of query rows walking the whole context), timed against ``ours``
+    (the full operator step) in interleaved CUDA-event samples with a
+    rotating order, the method of the reference's benchmarks/spike_triton_paged.py:309-415."""
+
+    import statistics as st
+
+    import torch
+
+    if batch.query.dtype != torch.float16:
+        return {"unavailable": "the reference's Triton operator supports torch.float16 only"}
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    try:
+        from micro_vllm.attention.operators.triton_paged import triton_paged_attention
+    except Exception as exc:  # micro_vllm or triton missing
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+    md = batch.metadata
+
+    def theirs():
+        return triton_paged_attention(batch.query, batch.key, batch.value, batch.cache, md)
+
+    out_ref, out_ours = theirs(), ours()
+    torch.cuda.synchronize(dev)
+    diff = (out_ref.float() - out_ours.float()).abs().max().item()
+    ops = {"ours": ours, "triton": theirs}
+    for _ in range(3):
+        for fn in ops.values():
+            fn()
+    torch.cuda.synchronize(dev)
+    times = {name: [] for name in ops}
+    names = list(ops)
+    for i in range(samples):
+        for name in names[i % 2:] + names[:i % 2]:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(launches):
+                ops[name]()
+            b.record()
+            b.synchronize()
+            times[name].append(a.elapsed_time(b) / launches)
+    t_ours, t_theirs = st.median(times["ours"]), st.median(times["triton"])
+    return {
+        "impl": "triton_paged_attention, the reference's Triton kernel (KV write + paged attention), "
+                "compiled here by Triton for this GPU",
+        "ms_per_step": t_theirs,
+        "ours_ms_per_step": t_ours,
+        "speedup_ours_over_triton": t_theirs / t_ours,
+        "max_abs_diff_vs_ours": diff,
+        "method": f"interleaved CUDA-event samples, rotating order, {samples} samples x {launches} launches, "
+                  "medians",
+    }
+
+
 def run_ours(args) -> dict:
     import torch
     import torch.distributed as dist
@@ -429,6 +488,13 @@ def run_ours(args) -> dict:
     clock_info = clocks.stop()
     attn_ms = max_over_ranks(a_start.elapsed_time(a_stop) / args.steps)
 
+    # ---- the reference's own GPU kernel on the same batch (rank 0) ----
+    comparator = None
+    if rank == 0 and not args.no_triton:
+        comparator = triton_comparator(batch, step, dev)
+        torch.cuda.synchronize(dev)
+    barrier()
+
     # ---- end to end through the public operator with host buffers ----
     # The step's host inputs are packed into one pinned buffer (the
     # caller-side staging a serving loop keeps) and uploaded with one copy;
@@ -460,14 +526,16 @@ def run_ours(args) -> dict:
     staging = PinnedStaging(dev)
     staging.pack(host)
 
+    # Every step packs its host inputs into pinned memory (the caller-side
+    # staging of a serving loop) inside the timed region, then uploads them.
     def serial_step(i: int) -> None:
+        staging.pack(host)
         out_hosts[0].copy_(run_op(staging.upload()), non_blocking=True)
 
     pipe = UploadPipeline(dev)
-    pipe.slot(0).pack(host)
-    pipe.slot(1).pack(host)
 
     def pipelined_step(i: int) -> None:
+        pipe.slot(i).pack(host)
         out = run_op(pipe.upload(i))
         pipe.download(i, out, out_hosts[i % 2])
 
@@ -548,17 +616,23 @@ def run_ours(args) -> dict:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "ms_per_step": e2e_ms,
-            "what": "B200PagedAttentionOperator.forward on this step's q/k/v and metadata uploaded from one "
-                    "pinned host buffer (one copy), output read back to pinned host memory; uploads and "
-                    "read-backs pipelined against the neighbouring steps' kernels (UploadPipeline)",
+            "what": "B200PagedAttentionOperator.forward on this step's q/k/v and metadata, packed from "
+                    "pageable host tensors into one pinned buffer and uploaded with one copy, output read "
+                    "back to pinned host memory, all inside the timed region; packing and copies of step "
+                    "i+1 / i-1 overlap step i's kernels (UploadPipeline)",
             "serial": {"value": step_bytes_all / (serial_ms * 1e-3) / 1e9, "ms_per_step": serial_ms,
-                       "what": "the same copies and step one after the other on one stream"},
+                       "what": "the same packing, copies and step one after the other on one stream"},
         },
         "gpu_launches": 4 * args.steps * world,
         "clocks": clock_info,
     }
     if world > 1:
         line["config"]["shard_imbalance"] = max(s.work for s in shards) / (sum(s.work for s in shards) / world)
+    if comparator is not None:
+        if "ms_per_step" in comparator:
+            comparator["value"] = attn_bytes / (comparator["ms_per_step"] * 1e-3) / 1e9
+            comparator["unit"] = "GB/s"
+        line["reference_gpu"] = comparator
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, elsize, args.cpu_sample_seconds)
     return line
@@ -582,7 +656,7 @@ def _engine_config(path, operator: str, graphs: bool, args):
     )
 
 
-def _engine_once(name: str, operator: str, graphs: bool, options, requests, args, dev) -> dict:
+def _engine_once(name: str, operator: str, graphs: bool, options, requests, args, dev, then=None) -> dict:
     """Initialise one worker, warm it with a short run, then time the
     requests to completion through a fresh Engine."""
 
@@ -592,9 +666,10 @@ def _engine_once(name: str, operator: str, graphs: bool, options, requests, args
     from micro_vllm_b200.engine import build_worker, fresh_engine, run_engine
 
     # Every rank takes the same collectives whatever fails: one MIN after
-    # the set-up (also the start barrier of the timed run), none inside it.
+    # the set-up (the start barrier of the timed run) and, with a second
+    # run, one MAX before it (its start barrier); none inside the runs.
     t0 = time.perf_counter()
-    worker = config = None
+    worker = config = run = second = None
     error = None
     try:
         config = _engine_config(ENGINE_CHECKPOINT, operator, graphs, args)
@@ -606,17 +681,31 @@ def _engine_once(name: str, operator: str, graphs: bool, options, requests, args
     init_s = time.perf_counter() - t0
     try:
         if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
-            raise RuntimeError(error or "another rank failed to set up its engine")
-        run = run_engine(fresh_engine(worker, config), requests, dev)
+            error = error or "another rank failed to set up its engine"
+        else:
+            try:
+                run = run_engine(fresh_engine(worker, config), requests, dev)
+            except Exception as exc:
+                error = f"{type(exc).__name__}: {exc}"
+        if then is not None:
+            _reduce(0.0, "max", dev)
+            if error is None:
+                try:
+                    second = run_engine(fresh_engine(worker, config), then, dev)
+                except Exception as exc:
+                    error = f"{type(exc).__name__}: {exc}"
     finally:
         if worker is not None:
             worker.shutdown()
         del worker
         gc.collect()
         torch.cuda.empty_cache()
+    if error is not None:
+        raise RuntimeError(error)
     return {"name": name, "seconds": run.seconds, "wall_seconds": run.wall_seconds, "steps": run.steps,
             "output_tokens": run.output_tokens, "prompt_tokens": run.prompt_tokens, "init_seconds": init_s,
-            "outputs": run.outputs}
+            "outputs": run.outputs,
+            **({"then": {"seconds": second.seconds, "output_tokens": second.output_tokens}} if second else {})}
 
 
 def engine_measure(args) -> dict:
@@ -647,12 +736,22 @@ def engine_measure(args) -> dict:
     if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
         return {"unavailable": error or "another rank could not prepare the engine"}
 
+    import torch
+
+    # Eight engine processes share the host: keep each one's CPU ops on a
+    # few threads (the scheduler and engine loop are single-threaded Python).
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
     requests = engine_requests(args.engine_requests, max_tokens=args.engine_max_tokens, seed=0)
     shards = partition_sequences([len(r.prompt_token_ids) + r.max_tokens for r in requests], world)
     mine = [requests[i] for i in shards[rank].indices]
-    result = None
+    # Weak scaling beside it: every replica serves its own stream of the
+    # same size (other seeds); at N=1 it is the same job.
+    own = engine_requests(args.engine_requests, max_tokens=args.engine_max_tokens, seed=1000 + rank)
+    result = weak = None
     try:
-        result = _engine_once("b200", "b200_paged", True, RunnerOptions(), mine, args, dev)
+        result = _engine_once("b200", "b200_paged", True, RunnerOptions(), mine, args, dev,
+                              then=own if world > 1 else None)
+        weak = result.pop("then", None)
     except Exception:
         error = traceback.format_exc(limit=3).strip().splitlines()[-1]
     if _reduce(0.0 if error else 1.0, "min", dev) < 1.0:
@@ -661,6 +760,16 @@ def engine_measure(args) -> dict:
     wall = _reduce(result["wall_seconds"], "max", dev)
     tokens = _reduce(float(result["output_tokens"]), "sum", dev)
     steps = _reduce(float(result["steps"]), "max", dev)
+    weak_line = None
+    if world > 1:
+        weak_seconds = _reduce(weak["seconds"], "max", dev)
+        weak_tokens = _reduce(float(weak["output_tokens"]), "sum", dev)
+        weak_line = {
+            "value": weak_tokens / weak_seconds, "unit": "tokens/s", "scaling": "weak",
+            "seconds": weak_seconds, "output_tokens": int(weak_tokens),
+            "what": f"each of the {world} replicas serves its own {len(own)} requests (same distribution, "
+                    "seed 1000 + rank): the N=1 job per GPU",
+        }
     out = {
         "metric": "engine output tokens/s (BASELINE config 5)",
         "value": tokens / seconds,
@@ -688,6 +797,8 @@ def engine_measure(args) -> dict:
         "timing": "CUDA events around each rank's Engine.step loop (synchronised at both ends), max over ranks; "
                   "wall_seconds is the host clock around the same loop",
     }
+    if weak_line is not None:
+        out["weak"] = weak_line
     if world == 1 and not args.no_engine_baselines:
         try:
             ref = _engine_once("triton_paged", "triton_paged", True, None, mine, args, dev)

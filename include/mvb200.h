@@ -52,6 +52,7 @@ extern "C" {
 #define MVB_STATUS_BLOCK_OUT_OF_RANGE 2  /* block id outside [0,num_blocks): key hidden */
 #define MVB_STATUS_POSITION_PAST_TABLE 4 /* position past its request's block ids: slot -1 */
 #define MVB_STATUS_INCONSISTENT_COUNTS 8 /* counts disagree with the sizes: padding only */
+#define MVB_STATUS_WAIT_TIMEOUT 16       /* a kernel's bounded wait ran out: its rows are undefined */
 
 /* Visibility specs of mvb_build_metadata (attention/spec.py). */
 #define MVB_SPEC_FULL 0           /* FullAttentionSpec: start 0                          */
@@ -158,10 +159,14 @@ MVB_API int mvb_attention_forward(const void* query, int64_t query_token_stride,
  * The scratch it needs lives in a 24 MiB region compiled into the library,
  * which every GPU that loads the library holds until the process exits.
  * Batches needing more (mvb_paged_attention_workspace_size above 24 MiB,
- * i.e. tens of thousands of requests) are rejected with
- * MVB_ERR_WORKSPACE_TOO_SMALL.  The first call on each device looks up the
- * region's device address (cudaGetSymbolAddress with that device current);
- * make that first call before any stream capture.  All calls share the
+ * i.e. tens of thousands of requests on the tensor-core path) are rejected
+ * with MVB_ERR_WORKSPACE_TOO_SMALL; the exact CUDA-core path (fp32, other
+ * head sizes) needs no scratch and takes any batch.  The first call on each
+ * device looks up the region's device address (cudaGetSymbolAddress with
+ * that device current) and keeps it for the life of the process; make that
+ * first call before any stream capture, and do not call this entry point
+ * after cudaDeviceReset on that device (the kept address would be stale).
+ * All calls share the
  * region: calls whose GPU work overlaps (different streams or host threads
  * on one device) race and must be serialised by the caller.
  */
@@ -178,6 +183,22 @@ MVB_API int mvb_paged_attention_no_alloc(const void* query, int64_t query_token_
                                          int64_t block_table_width, int64_t num_tokens,
                                          int64_t num_requests, int32_t num_q_heads, float scale,
                                          int32_t dtype, int32_t* status, void* stream);
+
+/*
+ * Test hook for the attention kernels' bounded waits (no counterpart in the
+ * reference project).
+ *
+ * Arms a one-shot stall for the next paged-decode launch issued from the
+ * calling host thread: the producer warp of decode CTA `cta` issues nothing
+ * for the `tile`-th 16-token tile of its share (no copy is in flight for that
+ * stage, so nothing is withheld from a copy in progress), and every mbarrier
+ * wait of that launch gives up after `wait_limit` polls.  The consumers'
+ * wait for the skipped tile runs out: the launch sets MVB_STATUS_WAIT_TIMEOUT
+ * in its status word, lets the copies it issued land and returns, and the
+ * context stays usable; rows of that launch are undefined.  The next launch
+ * runs normally.  wait_limit <= 0 disarms.  Returns MVB_OK.
+ */
+MVB_API int mvb_debug_arm_decode_stall(int32_t cta, int32_t tile, int32_t wait_limit);
 
 /*
  * Fused Qwen3 attention prologue: per-head RMSNorm of query and key, rotary

@@ -27,6 +27,7 @@ MVB_STATUS_SLOT_OUT_OF_RANGE = 1
 MVB_STATUS_BLOCK_OUT_OF_RANGE = 2
 MVB_STATUS_POSITION_PAST_TABLE = 4
 MVB_STATUS_INCONSISTENT_COUNTS = 8
+MVB_STATUS_WAIT_TIMEOUT = 16
 
 MVB_SPEC_FULL = 0
 MVB_SPEC_SLIDING_WINDOW = 1
@@ -47,6 +48,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _I64, _I32, _P, _P],
     ),
     "mvb_paged_attention_workspace_size": (_SZ, [_I64, _I64, _I32, _I32, _I32]),
+    "mvb_debug_arm_decode_stall": (ctypes.c_int, [_I32, _I32, _I32]),
     "mvb_paged_attention": (
         ctypes.c_int,
         [

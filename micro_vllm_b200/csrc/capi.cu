@@ -64,6 +64,10 @@ const char* mvb_status_string(int status) {
 
 int mvb_last_cuda_error(void) { return g_last_cuda_error; }
 
+int mvb_debug_arm_decode_stall(int32_t cta, int32_t tile, int32_t wait_limit) {
+  return arm_decode_stall(cta, tile, wait_limit);
+}
+
 int mvb_reshape_and_cache(const void* key, const int64_t* key_strides, const void* value,
                           const int64_t* value_strides, void* kv_cache, int64_t num_blocks,
                           int32_t block_size, int32_t num_kv_heads, int32_t head_dim,

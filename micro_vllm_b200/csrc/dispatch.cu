@@ -1,5 +1,7 @@
 // run_paged_attention: picks the kernels for one call and carves the
 // caller's workspace.  Nothing here touches device memory from the host.
+#include <mutex>
+
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
 
@@ -49,17 +51,22 @@ size_t workspace_bytes_for(int64_t max_tokens, int64_t max_requests, int32_t num
 }
 
 int num_sms() {
-  static int cached_device = -1, cached = 0;
+  // One entry per device, filled under a lock: host threads driving
+  // different devices may call at the same time.
+  static std::mutex lock;
+  static int cached[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev != cached_device) {
+  const bool slot = dev >= 0 && dev < kMaxDevices;
+  std::lock_guard<std::mutex> guard(lock);
+  if (!slot || cached[dev] == 0) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    cached = n;
-    cached_device = dev;
+    if (!slot) return n;
+    cached[dev] = n;
   }
-  return cached;
+  return cached[dev];
 }
 
 int run_paged_attention(const AttentionProblem& p) {

@@ -44,11 +44,13 @@ constexpr int kDecodeHeadDim = 128;
 constexpr int kMaxHeadsPerCta = 8;
 // Upper bound on decode CTAs (one or two per SM); sizes the partial area.
 constexpr int kMaxDecodeCtas = 320;
+// Devices the per-device host caches (SM count, grids, kernel attributes) keep.
+constexpr int kMaxDevices = 64;
 // Longest context a request may have (2^30 tokens).
 constexpr int64_t kMaxContext = (int64_t)1 << 30;
 
 // Status bit for a bounded wait that ran out (a kernel bug, never expected).
-constexpr int32_t kStatusWaitTimeout = 4;
+constexpr int32_t kStatusWaitTimeout = MVB_STATUS_WAIT_TIMEOUT;
 
 // ctrl[] words (int64).
 enum CtrlWord : int {
@@ -85,6 +87,8 @@ int launch_paged_attention_generic(const AttentionProblem& p, const int32_t* kin
 int heads_per_cta(int32_t num_kv_heads);
 // Decode grid for this device and problem (also what the planner assumes).
 int decode_grid(const AttentionProblem& p, int* smem_bytes);
+// Arms the one-shot decode stall of mvb_debug_arm_decode_stall for this host thread.
+int arm_decode_stall(int32_t cta, int32_t tile, int32_t wait_limit);
 
 // True when the tensor-core prefill kernel can take this problem (head_dim
 // 128, fp16/bf16, group dividing 128, pages of a multiple of 16 tokens,

@@ -13,9 +13,12 @@
 //
 // On the host the array's name is only a stand-in, not a device address, so
 // the first call on each device looks up the array's real device address
-// with cudaGetSymbolAddress (with that device current) and caches it.  That
-// first call should come before any stream capture.  Every call then shares
-// the same region and leaves its contents behind; the kernels re-derive
+// with cudaGetSymbolAddress (with that device current) and caches it for the
+// life of the process.  That first call should come before any stream
+// capture.  The cached address belongs to the device's primary context:
+// after cudaDeviceReset, or once the primary context has been released and
+// created again, it is stale and this entry point must not be called.
+// Every call shares the same region and leaves its contents behind; the kernels re-derive
 // everything they read from it on each call (the planner rewrites its arrays
 // and zeroes the merge counters and the zero row before the decode kernel
 // starts), so no state carries over.  Two calls whose work overlaps on the
@@ -29,11 +32,10 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = (size_t)24 << 20;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_no_alloc_scratch[kNoAllocScratchBytes];
 
-void* g_scratch_device_ptr[kMaxDevices] = {};
+void* g_scratch_device_ptr[mvb::kMaxDevices] = {};
 std::mutex g_scratch_mutex;
 
 }  // namespace
@@ -46,19 +48,18 @@ extern "C" MVB_API int mvb_paged_attention_no_alloc(
     const int64_t* block_table, int64_t block_table_row_stride, int64_t block_table_width,
     int64_t num_tokens, int64_t num_requests, int32_t num_q_heads, float scale, int32_t dtype,
     int32_t* status, void* stream) {
-  if (num_requests < 0 || num_tokens < 0 || num_kv_heads <= 0) return MVB_ERR_INVALID_ARGUMENT;
-  // The batch must fit the built-in region (the same layout a caller-provided
-  // workspace would get).
-  if (mvb::workspace_layout(num_requests, num_tokens, num_kv_heads).end > kNoAllocScratchBytes)
-    return MVB_ERR_WORKSPACE_TOO_SMALL;
-
+  // Arguments are checked, and the batch is measured against the region, by
+  // mvb_paged_attention itself: the tensor-core path lays out its workspace in
+  // the region and answers MVB_ERR_WORKSPACE_TOO_SMALL when the batch needs
+  // more than kNoAllocScratchBytes; the exact CUDA-core path (fp32, other head
+  // sizes, unaligned views) uses no workspace and takes any batch.
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) {
     mvb::set_last_cuda_error(err);
     return MVB_ERR_CUDA;
   }
-  if (device < 0 || device >= kMaxDevices) return MVB_ERR_INVALID_ARGUMENT;
+  if (device < 0 || device >= mvb::kMaxDevices) return MVB_ERR_INVALID_ARGUMENT;
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_scratch_mutex);

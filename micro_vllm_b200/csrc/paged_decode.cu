@@ -35,6 +35,7 @@
 // HBM bandwidth).
 #include <math.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "mvb_common.cuh"
@@ -47,7 +48,7 @@ constexpr int kTile = 16;
 constexpr int kStages = 3;
 constexpr int kWin = 256;  // block-table entries the producer keeps in shared memory
 constexpr int kHeadRow = kDecodeHeadDim * 2;  // bytes of one head's row
-constexpr int kWaitLimit = 1 << 22;
+constexpr int kWaitLimit = 1 << 22;  // polls of a normal launch's waits
 
 struct DecodeParams {
   const char* query;
@@ -68,6 +69,8 @@ struct DecodeParams {
   float* partial_o;    // [kMaxDecodeCtas][2][8 heads][8 cols][128]
   float2* partial_ml;  // [kMaxDecodeCtas][2][8 heads][8 cols] (max, sum)
   int32_t* status;
+  int32_t wait_limit;  // polls before a wait gives up
+  int32_t stall_cta, stall_tile;  // test hook: that CTA's producer skips that tile (-1: none)
 };
 
 // ------------------------------------------------------------------ PTX
@@ -96,8 +99,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false (and the status bit) when the barrier never flips.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
-  for (int i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status,
+                                          int32_t limit) {
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (status != nullptr) atomicOr(status, kStatusWaitTimeout);
   return false;
@@ -186,7 +190,26 @@ struct Slot {  // per-stage header written by the producer
   int32_t pad;
 };
 
+// Waits (bounded) for the full barriers of the last kStages tiles issued
+// before tile k, skipping none: a stage whose copy was never issued simply
+// times out.
+__device__ __forceinline__ void drain_issued(uint32_t full0, int k, int32_t limit) {
+  for (int i = k - kStages > 0 ? k - kStages : 0; i < k; ++i)
+    mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, nullptr, limit);
+}
+
+// Polls of a wait: the constant kWaitLimit in a normal launch, the armed
+// limit in the stall-hook instantiation.
+template <bool kHook>
+__device__ __forceinline__ int32_t wait_limit(const DecodeParams& p) {
+  return kHook ? p.wait_limit : kWaitLimit;
+}
+
 // ------------------------------------------------------------ producer
+// kHook: the instantiation launched only when mvb_debug_arm_decode_stall armed
+// a stall (waits bounded by the armed limit, one tile skipped); normal
+// launches run kHook = false.
+template <bool kHook>
 __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
                         uint8_t* ring, Slot* slots, uint32_t full0, uint32_t empty0,
                         int32_t stage_bytes, int32_t plane_stride, int32_t rowp, int64_t* win) {
@@ -201,6 +224,7 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
   const int64_t* trow = p.table + r * p.table_stride;
   int64_t win_r = -1, win_lo = 0;  // request and first page held in win[]
   int k = 0;
+  bool stalled = false;
   for (int64_t x = first; x < last; ++x, ++k) {
     const int64_t g = x / tiles, local = x - g * tiles;
     if (g != group || local >= req_hi) {  // next request (skip those with no tiles)
@@ -247,12 +271,18 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
     }
     const int64_t raw_blk = need ? win[lb - win_lo] : 0;  // checked after the wait
     const int s = k % kStages;
-    if (!mbar_wait(empty0 + 8 * s, ((k / kStages) & 1) ^ 1, p.status)) {
+    if (!mbar_wait(empty0 + 8 * s, ((k / kStages) & 1) ^ 1, p.status, wait_limit<kHook>(p))) {
       // A consumer stopped: let the copies already issued land before the
       // CTA leaves (each wait is bounded again).
-      for (int i = k - kStages > 0 ? k - kStages : 0; i < k; ++i)
-        mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, nullptr);
+      drain_issued(full0, k, wait_limit<kHook>(p));
       return;
+    }
+    if (kHook && k == p.stall_tile && (int)blockIdx.x == p.stall_cta) {
+      // Test hook (mvb_debug_arm_decode_stall): nothing is issued for this
+      // tile, so its stage never fills and the consumers' wait for it runs
+      // out; no copy is in flight for it.
+      stalled = true;
+      continue;
     }
     const int64_t blk = !in_extent ? -2
                         : (in_table && raw_blk >= 0 && raw_blk < p.num_blocks) ? raw_blk : -1;
@@ -271,10 +301,15 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
     bulk_g2s(smem_u32(ring + s * stage_bytes + plane * plane_stride + row * rowp), src, copy_bytes,
              full0 + 8 * s);
   }
+  // The copies of the last stages have landed before the CTA may exit.  In a
+  // normal launch the consumers waited for them already (the probes succeed
+  // at once); after a stall the consumers left early and this drain is what
+  // keeps the CTA alive until its copies are done.
+  if (kHook && stalled) drain_issued(full0, k, wait_limit<kHook>(p));
 }
 
 // ------------------------------------------------------------ consumer
-template <typename T>
+template <typename T, bool kHook>
 __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
                         int64_t n_all, const uint8_t* ring, const Slot* slots, uint32_t full0,
                         uint32_t empty0, int32_t stage_bytes, int32_t plane_stride, int32_t rowp) {
@@ -293,7 +328,7 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
   int k = 0;
   for (int64_t x = first; x < last; ++x, ++k) {
     const int s = k % kStages;
-    if (!mbar_wait(full0 + 8 * s, (k / kStages) & 1, p.status)) return;
+    if (!mbar_wait(full0 + 8 * s, (k / kStages) & 1, p.status, wait_limit<kHook>(p))) return;
     const Slot slot = slots[s];
     if (slot.vr != cur_vr) {  // a new request segment starts in this CTA
       cur_vr = slot.vr;
@@ -485,6 +520,9 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     for (int64_t b = b_first; b <= b_last; ++b)
       nseg += (b * n_all / grid) < ((b + 1) * n_all / grid);
     if (done != nseg - 1) continue;
+    // Every segment has counted: the counter goes back to zero for the next
+    // launch over the same plan.
+    if (lane == 0) p.merge_count[r * p.num_kv_heads + kvh] = 0;
     // Last segment to finish: merge all segments of (request, kvh).  The
     // segments' (max, sum) pairs are loaded one per lane and combined with
     // shuffles; the partial O rows are then read several at a time, so the
@@ -608,7 +646,7 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
   }
 }
 
-template <typename T>
+template <typename T, bool kHook>
 __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
     paged_decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t ring[];
@@ -636,16 +674,23 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
   if (first >= last) return;
   const int warp = threadIdx.x >> 5;
   if (warp == hb) {
-    produce(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride, rowp,
+    produce<kHook>(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride,
+                   rowp,
             table_win);
   } else {
-    consume<T>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
+    consume<T, kHook>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
                plane_stride, rowp);
   }
 }
 
+// The dynamic shared-memory limit is a property of the kernel function on a
+// device, shared by every heads-per-CTA configuration: it is always set to
+// the largest ring (kMaxHeadsPerCta), so a launch with a smaller ring never
+// lowers it below what a larger one needs.
 int set_up(const void* fn, int smem, int threads, int* per_sm) {
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  constexpr int kLargestRing = kStages * 2 * kTile * (kMaxHeadsPerCta * kHeadRow + 16);
+  cudaError_t e =
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLargestRing);
   if (e == cudaSuccess)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, fn, threads, smem);
   if (e != cudaSuccess) {
@@ -657,6 +702,18 @@ int set_up(const void* fn, int smem, int threads, int* per_sm) {
 
 }  // namespace
 
+// The stall armed by mvb_debug_arm_decode_stall for this host thread's next
+// decode launch.
+struct StallHook {
+  int32_t cta = -1, tile = -1, wait_limit = 0;
+};
+thread_local StallHook g_stall;
+
+int arm_decode_stall(int32_t cta, int32_t tile, int32_t wait_limit) {
+  g_stall = wait_limit > 0 ? StallHook{cta, tile, wait_limit} : StallHook{};
+  return MVB_OK;
+}
+
 int heads_per_cta(int32_t num_kv_heads) {
   for (int hb = kMaxHeadsPerCta; hb > 1; --hb)
     if (num_kv_heads % hb == 0) return hb;
@@ -667,25 +724,39 @@ int decode_grid(const AttentionProblem& a, int* smem_bytes) {
   const int hb = heads_per_cta(a.num_kv_heads);
   const int smem = kStages * 2 * kTile * (hb * kHeadRow + 16);
   const int threads = 32 * (hb + 1);
-  static int cached_device = -1, cached_hb = -1, cached_grid = 0;
+  // Per device and heads-per-CTA, filled under a lock (host threads driving
+  // different devices may call at the same time); the kernel attributes are
+  // set on each device the first time it is seen.
+  static std::mutex lock;
+  static int cached[kMaxDevices][kMaxHeadsPerCta + 1] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev != cached_device || hb != cached_hb) {
+  const bool slot = dev >= 0 && dev < kMaxDevices;
+  std::lock_guard<std::mutex> guard(lock);
+  if (!slot || cached[dev][hb] == 0) {
     int per_sm_h = 0, per_sm_b = 0;
-    if (set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half>), smem, threads,
+    int per_sm_hook = 0;
+    if (set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half, false>), smem, threads,
                &per_sm_h) != MVB_OK ||
-        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16>), smem, threads,
-               &per_sm_b) != MVB_OK)
+        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, false>), smem,
+               threads, &per_sm_b) != MVB_OK ||
+        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half, true>), smem, threads,
+               &per_sm_hook) != MVB_OK ||
+        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, true>), smem,
+               threads, &per_sm_hook) != MVB_OK)
       return -1;
     int per_sm = per_sm_h < per_sm_b ? per_sm_h : per_sm_b;
     if (per_sm < 1) per_sm = 1;
     int grid = num_sms() * per_sm;
-    cached_grid = grid < kMaxDecodeCtas ? grid : kMaxDecodeCtas;
-    cached_device = dev;
-    cached_hb = hb;
+    grid = grid < kMaxDecodeCtas ? grid : kMaxDecodeCtas;
+    if (!slot) {
+      *smem_bytes = smem;
+      return grid;
+    }
+    cached[dev][hb] = grid;
   }
   *smem_bytes = smem;
-  return cached_grid;
+  return cached[dev][hb];
 }
 
 int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w, int32_t grid,
@@ -722,11 +793,22 @@ int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w, int
   dp.partial_o = reinterpret_cast<float*>(ws + w.partial_o);
   dp.partial_ml = reinterpret_cast<float2*>(ws + w.partial_ml);
   dp.status = a.status;
+  dp.wait_limit = kWaitLimit;
+  dp.stall_cta = dp.stall_tile = -1;
+  const bool hook = g_stall.wait_limit > 0;
+  if (hook) {  // one-shot test hook armed on this host thread
+    dp.wait_limit = g_stall.wait_limit;
+    dp.stall_cta = g_stall.cta;
+    dp.stall_tile = g_stall.tile;
+    g_stall = StallHook{};
+  }
   const int threads = 32 * (dp.heads_per_cta + 1);
   if (a.dtype == MVB_DTYPE_F16)
-    paged_decode_kernel<__half><<<grid, threads, smem_bytes, a.stream>>>(dp);
+    (hook ? paged_decode_kernel<__half, true>
+          : paged_decode_kernel<__half, false>)<<<grid, threads, smem_bytes, a.stream>>>(dp);
   else if (a.dtype == MVB_DTYPE_BF16)
-    paged_decode_kernel<__nv_bfloat16><<<grid, threads, smem_bytes, a.stream>>>(dp);
+    (hook ? paged_decode_kernel<__nv_bfloat16, true>
+          : paged_decode_kernel<__nv_bfloat16, false>)<<<grid, threads, smem_bytes, a.stream>>>(dp);
   else
     return MVB_ERR_UNSUPPORTED_DTYPE;
   return check_launch();

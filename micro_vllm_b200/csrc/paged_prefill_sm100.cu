@@ -61,6 +61,8 @@
 // (visible query-key pairs).
 #include <math.h>
 
+#include <mutex>
+
 #include <type_traits>
 
 #include "mvb_common.cuh"
@@ -859,18 +861,25 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
 
 EncodeTiled encoder() {
   static EncodeTiled fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<EncodeTiled>(ptr);
-  }
+  });
   return fn;
 }
+
+// Per-device host state of the prefill kernel, filled under one lock (host
+// threads driving different devices may call at the same time).
+struct PrefillDeviceState {
+  bool checked = false, fits = false, configured = false;
+};
+std::mutex g_prefill_lock;
+PrefillDeviceState g_prefill_state[kMaxDevices];
 
 }  // namespace
 
@@ -879,19 +888,20 @@ int prefill_tokens_per_unit(int32_t group) { return 2 * kRows / group; }
 // The kernel's registers allow a full 384-thread block on this device, and
 // it was built with exactly the per-thread count its register split assumes.
 bool prefill_kernel_fits() {
-  static int cached_device = -1;
-  static bool fits = false;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev != cached_device) {
+  if (dev < 0 || dev >= kMaxDevices) return false;
+  std::lock_guard<std::mutex> guard(g_prefill_lock);
+  PrefillDeviceState& st = g_prefill_state[dev];
+  if (!st.checked) {
     cudaFuncAttributes fa_h, fa_b;
-    fits = cudaFuncGetAttributes(&fa_h, paged_prefill_kernel<__half>) == cudaSuccess &&
-           cudaFuncGetAttributes(&fa_b, paged_prefill_kernel<__nv_bfloat16>) == cudaSuccess &&
-           fa_h.maxThreadsPerBlock >= kThreads && fa_b.maxThreadsPerBlock >= kThreads &&
-           fa_h.numRegs == kLaunchRegs && fa_b.numRegs == kLaunchRegs;
-    cached_device = dev;
+    st.fits = cudaFuncGetAttributes(&fa_h, paged_prefill_kernel<__half>) == cudaSuccess &&
+              cudaFuncGetAttributes(&fa_b, paged_prefill_kernel<__nv_bfloat16>) == cudaSuccess &&
+              fa_h.maxThreadsPerBlock >= kThreads && fa_b.maxThreadsPerBlock >= kThreads &&
+              fa_h.numRegs == kLaunchRegs && fa_b.numRegs == kLaunchRegs;
+    st.checked = true;
   }
-  return fits;
+  return st.fits;
 }
 
 bool prefill_tc_supported(const AttentionProblem& a) {
@@ -972,20 +982,24 @@ int launch_paged_prefill(const AttentionProblem& a, const WorkspaceLayout& w) {
   pp.unit_order = reinterpret_cast<const int32_t*>(ws + w.prefill_unit_order);
   pp.status = a.status;
 
-  static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_kernel<__half>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(paged_prefill_kernel<__nv_bfloat16>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return MVB_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return MVB_ERR_INVALID_ARGUMENT;
+  {
+    std::lock_guard<std::mutex> guard(g_prefill_lock);
+    PrefillDeviceState& st = g_prefill_state[dev];
+    if (!st.configured) {
+      cudaError_t e = cudaFuncSetAttribute(paged_prefill_kernel<__half>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_prefill_kernel<__nv_bfloat16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return MVB_ERR_CUDA;
+      }
+      st.configured = true;
     }
-    configured_device = dev;
   }
   const int grid = num_sms();
   if (a.dtype == MVB_DTYPE_BF16)

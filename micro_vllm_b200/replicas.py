@@ -6,13 +6,16 @@ the ranks with the ``spawn`` method (safe after CUDA initialisation), gives
 each the torch.distributed rendezvous environment, and watches them from the
 host: a rank that raises (non-zero exit code) or never finishes (join
 timeout, then terminate/kill) is reported in one ``ReplicaFailure`` instead
-of leaving the job hanging.  Collectives inside the ranks should use a short
-process-group timeout so survivors of a failed rank end with an error too.
+of leaving the job hanging.  The launcher waits on all ranks at once: the
+first rank to exit non-zero is reported at once and the others are stopped,
+even when they are blocked in a collective waiting for it.  Collectives
+inside the ranks should still use a short process-group timeout.
 """
 
 from __future__ import annotations
 
 import multiprocessing as mp
+from multiprocessing.connection import wait
 import os
 import socket
 import time
@@ -70,17 +73,27 @@ def launch_replicas(
         p.start()
     deadline = time.monotonic() + timeout
     failed: dict[int, str] = {}
-    for r, p in enumerate(procs):
-        p.join(max(0.0, deadline - time.monotonic()))
-    for r, p in enumerate(procs):
+    running = {p.sentinel: r for r, p in enumerate(procs)}
+    # Watch every rank at once: the first one to exit non-zero ends the job
+    # now, not after the ranks it leaves blocked in a collective time out.
+    while running and not failed:
+        left = deadline - time.monotonic()
+        if left <= 0:
+            break
+        for sentinel in wait(list(running), timeout=left):
+            r = running.pop(sentinel)
+            procs[r].join()
+            if procs[r].exitcode != 0:
+                failed[r] = f"exit code {procs[r].exitcode}"
+    first_failure = min(failed) if failed else None
+    for r in running.values():
+        p = procs[r]
+        failed[r] = (f"timed out after {timeout:.0f}s" if first_failure is None
+                     else f"stopped after rank {first_failure} failed")
+        p.terminate()
+        p.join(5)
         if p.is_alive():
-            failed[r] = f"timed out after {timeout:.0f}s"
-            p.terminate()
+            p.kill()
             p.join(5)
-            if p.is_alive():
-                p.kill()
-                p.join(5)
-        elif p.exitcode != 0:
-            failed[r] = f"exit code {p.exitcode}"
     if failed:
         raise ReplicaFailure(failed)

@@ -88,11 +88,14 @@ class UploadPipeline:
     once, or again before its step).  ``upload(i)`` copies slot i % 2 to the
     device on the upload stream, once the kernels that last read that slot's
     device buffer (step i - 2) have finished, and makes the current stream
-    wait for that copy alone; it returns the device views.  ``download(i,
-    result, host)`` reads the step's result back on the read-back stream once
-    the current stream has produced it.  ``drain()`` makes the current stream
-    wait for every copy issued so far.  Step i's kernels then overlap step
-    i + 1's upload and step i - 1's read-back.
+    wait for that copy alone; it returns the device views.  Step i's kernels
+    are the work the caller queues on the current stream between
+    ``upload(i)`` and ``upload(i + 1)``: ``upload(i + 1)`` marks their end as
+    the release of slot i % 2, whether or not the step read anything back.
+    ``download(i, result, host)`` reads the step's result back on the
+    read-back stream once the current stream has produced it.  ``drain()``
+    makes the current stream wait for every copy issued so far.  Step i's
+    kernels then overlap step i + 1's upload and step i - 1's read-back.
     """
 
     __slots__ = ("device", "_slots", "_h2d", "_d2h", "_released")
@@ -109,7 +112,12 @@ class UploadPipeline:
 
     def upload(self, i: int) -> dict[str, torch.Tensor]:
         compute = torch.cuda.current_stream(self.device)
+        # Everything queued so far (step i - 1's kernels, the last readers of
+        # the other slot's device buffer) releases that slot for step i + 1.
+        queued = torch.cuda.Event()
+        queued.record(compute)
         released = self._released[i % 2]
+        self._released[(i + 1) % 2] = queued
         if released is not None:
             self._h2d.wait_event(released)
         else:  # first use: after everything the caller queued so far
@@ -124,8 +132,7 @@ class UploadPipeline:
     def download(self, i: int, result: torch.Tensor, host: torch.Tensor) -> None:
         compute = torch.cuda.current_stream(self.device)
         done = torch.cuda.Event()
-        done.record(compute)  # this step's kernels, the last readers of its device buffer
-        self._released[i % 2] = done
+        done.record(compute)  # the step's result is complete
         self._d2h.wait_event(done)
         with torch.cuda.stream(self._d2h):
             host.copy_(result, non_blocking=True)

@@ -11,7 +11,7 @@ falling back here.
 Parity pin: ``tests/golden/make_golden.py`` ran the reference's own
 ``ReferenceAttentionOperator`` and ``write_kv_cache`` (imported from the
 reference source tree) on seeded inputs and stored inputs and outputs under
-``tests/golden/``; ``tests/test_oracle_golden.py`` checks this restatement
+``tests/golden/``; ``tests/test_oracle.py`` checks this restatement
 against those vectors and against the reference tests' known answers.
 
 Reference functions restated here (paths inside the reference project):

@@ -79,3 +79,21 @@ def hang_on_rank_one(rank: int, world_size: int) -> None:
     if rank == 1:
         time.sleep(600)
     dist.barrier()
+
+
+def fail_fast_while_rank_zero_waits(rank: int, world_size: int) -> None:
+    """Rank 1 fails at once; rank 0 blocks in a barrier with a long timeout."""
+
+    import torch.distributed as dist
+
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    dist.barrier()
+
+
+def sleep_on_rank_one(rank: int, world_size: int) -> None:
+    """Rank 1 never returns and takes no collective; rank 0 finishes."""
+
+    if rank == 1:
+        time.sleep(600)

@@ -116,6 +116,47 @@ def test_decode_batch_matches_oracle(dtype, num_q_heads, num_kv_heads) -> None:
     _run_and_check(batch)
 
 
+def test_config4_long_context_decode_matches_oracle() -> None:
+    """BASELINE config 4 on one GPU: 64 sequences at Hq 32 / Hkv 8 (group 4),
+    contexts U[4096, 8192], bf16, pages drawn over a 40 GB pool (block ids
+    past 2^19, byte offsets past 2^35).  The kernel runs the whole batch (the
+    stream-K shares cut long requests into many segments); a spread of rows
+    is checked against the oracle."""
+
+    ctx = uniform_lengths(64, 4096, 8192, seed=1000)
+    nb = int(40e9) // (2 * 16 * 8 * 128 * 2)
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=[1] * 64, num_q_heads=32, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=nb, dtype=torch.bfloat16, device=DEV, seed=2000,
+    )
+    order = sorted(range(64), key=lambda r: ctx[r])
+    rows = sorted(set(order[:4] + order[-4:] + list(range(0, 64, 4))))
+    _run_and_check(batch, rows)
+    del batch
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_config3_full_mixed_batch_matches_oracle(dtype) -> None:
+    """BASELINE config 3 at full size, in one call: 8 prefill chunks of 2048
+    new tokens over cached prefixes U[0, 1024] plus 120 decodes at contexts
+    U[256, 2048], 16/8/128 (the bench's seeds).  Checked: every decode and
+    the prefill chunks with the shortest and the longest prefix (every
+    token of each)."""
+
+    prefix = uniform_lengths(8, 0, 1024, seed=31)
+    dec_ctx = uniform_lengths(120, 256, 2048, seed=32)
+    ctx = [p + 2048 for p in prefix] + dec_ctx
+    qlen = [2048] * 8 + [1] * 120
+    nb = sum(-(-c // 16) for c in ctx) + 64
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=qlen, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=nb, dtype=dtype, device=DEV, seed=33,
+    )
+    rows = sorted({min(range(8), key=lambda r: prefix[r]), max(range(8), key=lambda r: prefix[r])}) + list(range(8, 128))
+    _run_and_check(batch, rows)
+
+
 @pytest.mark.parametrize("block_size", [1, 5, 8, 32, 64])
 def test_decode_any_block_size(block_size: int) -> None:
     ctx = uniform_lengths(12, 1, 700, seed=block_size)
@@ -364,6 +405,36 @@ def test_prefill_bf16_values_beyond_fp16_range() -> None:
     # Request 1 (fresh prompt): one written value past the fp16 maximum.
     batch.value[400 + 123, 5] = 9.0e4
     _run_and_check(batch)
+
+
+def test_a_decode_wait_that_runs_out_is_reported_and_the_next_call_is_correct() -> None:
+    """The kernels' bounded waits, exercised without a fault: a one-shot hook
+    (mvb_debug_arm_decode_stall) makes decode CTA 0's producer issue nothing
+    for the second tile of its share and limits every wait of that launch to
+    20 000 polls.  No copy is in flight for the skipped stage; the consumers'
+    wait for it runs out, the launch sets MVB_STATUS_WAIT_TIMEOUT, lets its
+    issued copies land and returns.  The context stays usable: the next call
+    on the same operator and workspace matches the oracle with a clean
+    status."""
+
+    ctx = uniform_lengths(48, 500, 2000, seed=5)
+    batch = paged_batch(
+        context_lengths=ctx, query_lengths=[1] * 48, num_q_heads=16, num_kv_heads=8, head_dim=128,
+        block_size=16, num_blocks=8000, dtype=torch.float16, device=DEV, seed=55,
+    )
+    op = B200PagedAttentionOperator()
+    lib = _lib.load()
+    assert op.read_status(DEV) == 0
+    assert lib.mvb_debug_arm_decode_stall(0, 1, 20000) == _lib.MVB_OK
+    op(batch.query, batch.key, batch.value, batch.cache, batch.metadata)
+    assert op.read_status(DEV) & _lib.MVB_STATUS_WAIT_TIMEOUT
+    _run_and_check(batch, op=op)
+    assert op.read_status(DEV) == 0
+    # Disarming works too: an armed-then-disarmed hook changes nothing.
+    assert lib.mvb_debug_arm_decode_stall(0, 1, 20000) == _lib.MVB_OK
+    assert lib.mvb_debug_arm_decode_stall(0, 1, 0) == _lib.MVB_OK
+    _run_and_check(batch, op=op)
+    assert op.read_status(DEV) == 0
 
 
 def test_prefill_repeated_calls_reuse_the_workspace() -> None:

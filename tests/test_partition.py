@@ -54,7 +54,9 @@ def test_a_failing_rank_is_reported() -> None:
 
     with pytest.raises(ReplicaFailure) as info:
         launch_replicas(fail_on_rank_one, 2, timeout=60)
-    assert set(info.value.failed) == {1}
+    assert info.value.failed[1].startswith("exit code")
+    # Rank 0 is either done already or stopped because rank 1 failed.
+    assert info.value.failed.get(0, "stopped after rank 1 failed") == "stopped after rank 1 failed"
 
 
 def test_a_hung_rank_is_detected_and_stopped() -> None:
@@ -62,6 +64,33 @@ def test_a_hung_rank_is_detected_and_stopped() -> None:
 
     with pytest.raises(ReplicaFailure) as info:
         launch_replicas(hang_on_rank_one, 2, timeout=20)
-    # Rank 1 never finished; rank 0's barrier timed out with an error.
-    assert "timed out" in info.value.failed[1]
-    assert 0 in info.value.failed
+    # Rank 1 never joins; rank 0's barrier times out with an error (exit
+    # code), which ends the job and stops rank 1.
+    assert info.value.failed[0].startswith("exit code")
+    assert info.value.failed[1] == "stopped after rank 0 failed"
+
+
+def test_a_rank_that_never_finishes_times_out() -> None:
+    """No collective to fail: the launcher's own deadline stops the rank."""
+
+    from _replica_worker import sleep_on_rank_one
+
+    with pytest.raises(ReplicaFailure) as info:
+        launch_replicas(sleep_on_rank_one, 2, timeout=8)
+    assert info.value.failed == {1: "timed out after 8s"}
+
+
+def test_an_early_failure_is_reported_before_the_timeout() -> None:
+    """Rank 1 exits non-zero at once while rank 0 waits in a collective: the
+    launcher reports it and stops rank 0 without waiting for the timeout."""
+
+    import time
+
+    from _replica_worker import fail_fast_while_rank_zero_waits
+
+    start = time.monotonic()
+    with pytest.raises(ReplicaFailure) as info:
+        launch_replicas(fail_fast_while_rank_zero_waits, 2, timeout=240)
+    assert time.monotonic() - start < 60
+    assert info.value.failed[1].startswith("exit code")
+    assert info.value.failed[0] == "stopped after rank 1 failed"

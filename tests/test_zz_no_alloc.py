@@ -80,9 +80,47 @@ def test_no_alloc_entry_point_matches_the_workspace_entry_point() -> None:
 def test_no_alloc_entry_point_rejects_batches_beyond_its_region() -> None:
     build()
     lib = _lib.load()
-    # Ten million requests need far more than the built-in 24 MiB.
+    # Ten million requests on the tensor-core path need far more than the
+    # built-in 24 MiB: refused before anything is launched, so small valid
+    # buffers stand in for the batch's.
+    buf = torch.zeros(1 << 16, dtype=torch.int64, device=DEV)
+    p = buf.data_ptr()
+    stream = torch.cuda.current_stream(DEV).cuda_stream
     rc = lib.mvb_paged_attention_no_alloc(
-        None, 0, 0, None, None, 1, 16, 8, 128, None, None, None, None, None, 0, 0,
-        1, 10_000_000, 16, 1.0, _lib.MVB_DTYPE_F16, None, None,
+        p, 2048, 128, p, p, 1, 16, 8, 128, p, p, p, p, p, 1, 1,
+        10_000_000, 10_000_000, 16, 1.0, _lib.MVB_DTYPE_F16, None, stream,
     )
     assert rc == _lib.MVB_ERR_WORKSPACE_TOO_SMALL
+    # Invalid arguments get the code mvb_paged_attention gives them, whatever the size.
+    for dtype, expected in ((7, _lib.MVB_ERR_UNSUPPORTED_DTYPE), (_lib.MVB_DTYPE_F16, _lib.MVB_ERR_INVALID_ARGUMENT)):
+        args = (None, 0, 0, None, None, 1, 16, 8, 128, None, None, None, None, None, 0, 0,
+                1, 10_000_000, 16, 1.0, dtype)
+        assert lib.mvb_paged_attention(*args, None, 0, None, None) == expected
+        assert lib.mvb_paged_attention_no_alloc(*args, None, None) == expected
+
+
+def test_no_alloc_entry_point_on_the_exact_path() -> None:
+    """fp32 and head_dim 64 run the exact CUDA-core kernel, which uses no
+    scratch: the no-allocation entry point gives the same rows."""
+
+    build()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    for dtype, head_dim in ((torch.float32, 128), (torch.float16, 64)):
+        batch = paged_batch(
+            context_lengths=uniform_lengths(12, 1, 600, seed=5) + [90], query_lengths=[1] * 12 + [30],
+            num_q_heads=8, num_kv_heads=2, head_dim=head_dim, block_size=16, num_blocks=1000,
+            dtype=dtype, device=DEV, seed=31,
+        )
+        args = list(_common_args(batch, batch.query))
+        code = {torch.float32: _lib.MVB_DTYPE_F32, torch.float16: _lib.MVB_DTYPE_F16}[dtype]
+        outs = []
+        for entry in ("mvb_paged_attention", "mvb_paged_attention_no_alloc"):
+            out = torch.full_like(batch.query, float("nan"))
+            args[3] = out.data_ptr()
+            args[-1] = code
+            tail = (None, 0, None, stream) if entry == "mvb_paged_attention" else (None, stream)
+            assert getattr(lib, entry)(*args, *tail) == _lib.MVB_OK
+            outs.append(out)
+        torch.cuda.synchronize(DEV)
+        torch.testing.assert_close(outs[1], outs[0], atol=0, rtol=0)
