@@ -1,11 +1,20 @@
 // Internal interfaces between the C-ABI layer, the planner and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
 namespace mvb {
+
+// cuTensorMapEncodeTiled, looked up once through the runtime's driver entry
+// point (nullptr when the driver lacks it).
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled tensor_map_encoder();
 
 int elem_bytes_of(int32_t dtype);
 

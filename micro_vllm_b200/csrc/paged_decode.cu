@@ -40,6 +40,7 @@
 
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
+#include "ptx_sm100.cuh"
 
 namespace mvb {
 namespace {
@@ -57,6 +58,7 @@ struct DecodeParams {
   const char* cache;
   int64_t plane_bytes;
   int64_t num_blocks;
+  int64_t num_slots;  // slots per plane: value rows follow the key rows in the page map
   int32_t block_size, bs_shift, num_kv_heads, heads_per_cta, group, num_q_heads;
   const int64_t *qpos, *qstart, *qsl, *ctx_len, *table;
   int64_t table_stride, table_width, num_requests;
@@ -209,10 +211,15 @@ __device__ __forceinline__ int32_t wait_limit(const DecodeParams& p) {
 // kHook: the instantiation launched only when mvb_debug_arm_decode_stall armed
 // a stall (waits bounded by the armed limit, one tile skipped); normal
 // launches run kHook = false.
-template <bool kHook>
-__device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
-                        uint8_t* ring, Slot* slots, uint32_t full0, uint32_t empty0,
-                        int32_t stage_bytes, int32_t plane_stride, int32_t rowp, int64_t* win) {
+// kPaged: a tile is one TMA load per plane through `kvmap` (block sizes
+// that are multiples of 16, so a tile's 16 rows lie in one page), landing
+// 128-byte swizzled; otherwise each lane copies one row with cp.async.bulk
+// into 16-byte padded rows.
+template <bool kHook, bool kPaged>
+__device__ void produce(const DecodeParams& p, const CUtensorMap* kvmap, int64_t first,
+                        int64_t last, int64_t tiles, uint8_t* ring, Slot* slots, uint32_t full0,
+                        uint32_t empty0, int32_t stage_bytes, int32_t plane_stride, int32_t rowp,
+                        int64_t* win) {
   const int lane = threadIdx.x & 31;
   const int hb = p.heads_per_cta;
   const int row = lane & 15, plane = lane >> 4;
@@ -257,8 +264,9 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
     const bool in_table = pos >= 0 && lb < p.table_width;
     // Page lookups come from a window of the request's block table that the
     // warp loads into shared memory with coalesced loads (once per request
-    // and per 256 pages), so no tile waits on a dependent global load.
-    const bool need = in_extent && in_table;
+    // and per 256 pages), so no tile waits on a dependent global load.  A
+    // paged tile needs its page whichever of its rows are visible.
+    const bool need = (kPaged || in_extent) && in_table;
     if (__any_sync(0xffffffffu, need && (r != win_r || lb < win_lo || lb >= win_lo + kWin))) {
       const int64_t lo0 = __shfl_sync(0xffffffffu, lb, 0);  // row 0 holds the tile's first page
       for (int j = lane; j < kWin; j += 32) {
@@ -284,8 +292,8 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
       stalled = true;
       continue;
     }
-    const int64_t blk = !in_extent ? -2
-                        : (in_table && raw_blk >= 0 && raw_blk < p.num_blocks) ? raw_blk : -1;
+    const bool page_ok = in_table && raw_blk >= 0 && raw_blk < p.num_blocks;
+    const int64_t blk = !in_extent ? -2 : page_ok ? raw_blk : -1;
     const bool valid = blk >= 0;
     if (blk == -1 && p.status != nullptr) atomicOr(p.status, MVB_STATUS_BLOCK_OUT_OF_RANGE);
     const uint32_t mask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
@@ -294,6 +302,19 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
       mbar_expect_tx(full0 + 8 * s, 2 * kTile * copy_bytes);
     }
     __syncwarp();
+    if constexpr (kPaged) {
+      // The tile's 16 rows are slots off .. off + 15 of one page (page 0
+      // stands in for a missing one; its rows are masked and zeroed).
+      if (lane == 0) {
+        const int64_t slot0 = (page_ok ? raw_blk : 0) * p.block_size + off;
+        const uint32_t dst = smem_u32(ring + s * stage_bytes);
+        const int32_t seg0 = (int32_t)(2 * group * hb);
+        sm100::tma_load_3d(dst, kvmap, 0, (int32_t)slot0, seg0, full0 + 8 * s);
+        sm100::tma_load_3d(dst + plane_stride, kvmap, 0, (int32_t)(p.num_slots + slot0), seg0,
+                           full0 + 8 * s);
+      }
+      continue;
+    }
     const char* src =
         valid ? p.cache + plane * p.plane_bytes +
                     ((blk * p.block_size + off) * p.num_kv_heads + group * hb) * kHeadRow
@@ -309,7 +330,7 @@ __device__ void produce(const DecodeParams& p, int64_t first, int64_t last, int6
 }
 
 // ------------------------------------------------------------ consumer
-template <typename T, bool kHook>
+template <typename T, bool kHook, bool kPaged>
 __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int64_t tiles,
                         int64_t n_all, const uint8_t* ring, const Slot* slots, uint32_t full0,
                         uint32_t empty0, int32_t stage_bytes, int32_t plane_stride, int32_t rowp) {
@@ -371,21 +392,57 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
     }
 
     // ---- one 16-token tile of KV head kvh ----
-    const uint32_t kb = smem_u32(ring + s * stage_bytes) + w * kHeadRow;
-    const uint32_t vb = kb + plane_stride;
     // The tile's K and V fragments go to registers first, and the stage is
     // released before any math: the producer refills it while this warp
     // computes, so a stage is held for the 16 loads, not the whole tile.
     uint32_t ka[8][4], va[8][4];
+    if constexpr (kPaged) {
+      // Plane layout: [2 hb segments of 64 elements][16 rows][128 B], each
+      // 128-byte row with its 16-byte chunks XOR-swizzled by (row & 7), so
+      // the 8 rows of an ldmatrix read fall in 8 different bank groups.
+      // This warp's head owns segments 2w (dims 0-63) and 2w + 1.
+      const uint32_t kb = smem_u32(ring + s * stage_bytes) + (uint32_t)(2 * w * kTile * 128);
+      const uint32_t vb = kb + plane_stride;
+      if (slot.row_mask != 0xffffu) {
+        // Rows no query may see hold stale bytes of the page (or a stand-in
+        // page): zero their values so 0 x NaN cannot reach O.
+        uint8_t* vrows = const_cast<uint8_t*>(ring) + s * stage_bytes + plane_stride + 2 * w * kTile * 128;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-      ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, ka[ks]);
-    }
+        for (int j = 0; j < 8; ++j) {
+          const int i = lane + 32 * j;  // (half, row, chunk) = (i / 128, i / 8 % 16, i % 8)
+          const int row = (i >> 3) & 15;
+          if (!((slot.row_mask >> row) & 1u))
+            *reinterpret_cast<uint4*>(vrows + (i >> 7) * kTile * 128 + row * 128 + (i & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+        sm100::fence_proxy_async();  // ordered before the next TMA write of this stage
+        __syncwarp();
+      }
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int row = (lane & 7) + (lane >> 4) * 8;
-      ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, va[mt]);
+      for (int ks = 0; ks < 8; ++ks) {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int chunk = 2 * (ks & 3) + (lane >> 4);
+        ldsm_x4(kb + (uint32_t)(((ks >> 2) * kTile + row) * 128 + ((chunk ^ (row & 7)) << 4)), ka[ks]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int row = (lane & 7) + (lane >> 4) * 8;
+        const int chunk = 2 * (mt & 3) + ((lane >> 3) & 1);
+        ldsm_x4_t(vb + (uint32_t)(((mt >> 2) * kTile + row) * 128 + ((chunk ^ (row & 7)) << 4)), va[mt]);
+      }
+    } else {
+      const uint32_t kb = smem_u32(ring + s * stage_bytes) + w * kHeadRow;
+      const uint32_t vb = kb + plane_stride;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        ldsm_x4(kb + row * rowp + (2 * ks + (lane >> 4)) * 16, ka[ks]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int row = (lane & 7) + (lane >> 4) * 8;
+        ldsm_x4_t(vb + row * rowp + (2 * mt + ((lane >> 3) & 1)) * 16, va[mt]);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);  // release: orders the loads above first
@@ -646,15 +703,19 @@ __device__ void consume(const DecodeParams& p, int64_t first, int64_t last, int6
   }
 }
 
-template <typename T, bool kHook>
+template <typename T, bool kHook, bool kPaged>
 __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
-    paged_decode_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t ring[];
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kvmap, const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t ring_raw[];
+  // Swizzled TMA destinations want 1024-byte alignment (the launch adds the slack).
+  uint8_t* ring = kPaged ? reinterpret_cast<uint8_t*>(
+                               (reinterpret_cast<uintptr_t>(ring_raw) + 1023) & ~(uintptr_t)1023)
+                         : ring_raw;
   __shared__ __align__(8) uint64_t bars[2 * kStages];
   __shared__ Slot slots[kStages];
   __shared__ int64_t table_win[kWin];
   const int hb = p.heads_per_cta;
-  const int32_t rowp = hb * kHeadRow + 16;
+  const int32_t rowp = kPaged ? hb * kHeadRow : hb * kHeadRow + 16;
   const int32_t plane_stride = kTile * rowp;
   const int32_t stage_bytes = 2 * plane_stride;
   const int64_t tiles = p.ctrl[kCtrlTiles];
@@ -674,12 +735,11 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
   if (first >= last) return;
   const int warp = threadIdx.x >> 5;
   if (warp == hb) {
-    produce<kHook>(p, first, last, tiles, ring, slots, full0, empty0, stage_bytes, plane_stride,
-                   rowp,
-            table_win);
+    produce<kHook, kPaged>(p, &kvmap, first, last, tiles, ring, slots, full0, empty0, stage_bytes,
+                           plane_stride, rowp, table_win);
   } else {
-    consume<T, kHook>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
-               plane_stride, rowp);
+    consume<T, kHook, kPaged>(p, first, last, tiles, n_all, ring, slots, full0, empty0, stage_bytes,
+                              plane_stride, rowp);
   }
 }
 
@@ -720,6 +780,27 @@ int heads_per_cta(int32_t num_kv_heads) {
   return 1;
 }
 
+// The kernel's instantiations: dtype x stall hook x paged (TMA) tiles.
+using DecodeKernel = void (*)(const CUtensorMap, const DecodeParams);
+template <typename T>
+DecodeKernel kernel_for(bool hook, bool paged) {
+  return hook ? (paged ? paged_decode_kernel<T, true, true> : paged_decode_kernel<T, true, false>)
+              : (paged ? paged_decode_kernel<T, false, true> : paged_decode_kernel<T, false, false>);
+}
+const void* const* kernel_instances() {
+  static const void* fns[8] = {
+      reinterpret_cast<const void*>(kernel_for<__half>(false, false)),
+      reinterpret_cast<const void*>(kernel_for<__half>(false, true)),
+      reinterpret_cast<const void*>(kernel_for<__half>(true, false)),
+      reinterpret_cast<const void*>(kernel_for<__half>(true, true)),
+      reinterpret_cast<const void*>(kernel_for<__nv_bfloat16>(false, false)),
+      reinterpret_cast<const void*>(kernel_for<__nv_bfloat16>(false, true)),
+      reinterpret_cast<const void*>(kernel_for<__nv_bfloat16>(true, false)),
+      reinterpret_cast<const void*>(kernel_for<__nv_bfloat16>(true, true)),
+  };
+  return fns;
+}
+
 int decode_grid(const AttentionProblem& a, int* smem_bytes) {
   const int hb = heads_per_cta(a.num_kv_heads);
   const int smem = kStages * 2 * kTile * (hb * kHeadRow + 16);
@@ -734,18 +815,15 @@ int decode_grid(const AttentionProblem& a, int* smem_bytes) {
   const bool slot = dev >= 0 && dev < kMaxDevices;
   std::lock_guard<std::mutex> guard(lock);
   if (!slot || cached[dev][hb] == 0) {
-    int per_sm_h = 0, per_sm_b = 0;
-    int per_sm_hook = 0;
-    if (set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half, false>), smem, threads,
-               &per_sm_h) != MVB_OK ||
-        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, false>), smem,
-               threads, &per_sm_b) != MVB_OK ||
-        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__half, true>), smem, threads,
-               &per_sm_hook) != MVB_OK ||
-        set_up(reinterpret_cast<const void*>(paged_decode_kernel<__nv_bfloat16, true>), smem,
-               threads, &per_sm_hook) != MVB_OK)
-      return -1;
-    int per_sm = per_sm_h < per_sm_b ? per_sm_h : per_sm_b;
+    // Every instantiation gets the attribute; the grid follows the lowest
+    // occupancy among them (one CTA per SM for every head count here).
+    int per_sm = 1 << 30;
+    const void* const* fns = kernel_instances();
+    for (int i = 0; i < 8; ++i) {
+      int n = 0;
+      if (set_up(fns[i], smem, threads, &n) != MVB_OK) return -1;
+      per_sm = n < per_sm ? n : per_sm;
+    }
     if (per_sm < 1) per_sm = 1;
     int grid = num_sms() * per_sm;
     grid = grid < kMaxDecodeCtas ? grid : kMaxDecodeCtas;
@@ -803,14 +881,33 @@ int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w, int
     g_stall = StallHook{};
   }
   const int threads = 32 * (dp.heads_per_cta + 1);
-  if (a.dtype == MVB_DTYPE_F16)
-    (hook ? paged_decode_kernel<__half, true>
-          : paged_decode_kernel<__half, false>)<<<grid, threads, smem_bytes, a.stream>>>(dp);
-  else if (a.dtype == MVB_DTYPE_BF16)
-    (hook ? paged_decode_kernel<__nv_bfloat16, true>
-          : paged_decode_kernel<__nv_bfloat16, false>)<<<grid, threads, smem_bytes, a.stream>>>(dp);
-  else
-    return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (a.dtype != MVB_DTYPE_F16 && a.dtype != MVB_DTYPE_BF16) return MVB_ERR_UNSUPPORTED_DTYPE;
+  // Paged tiles (one TMA load per plane and tile) when a tile's 16 rows lie
+  // in one page and the map's 32-bit slot coordinate reaches both planes.
+  // The map views the cache as [2 * slots][2 * Hkv segments][64 elements]:
+  // a box of {64, 16 slots, 2 hb segments} is one tile of the CTA's heads,
+  // laid out segment-major in shared memory.
+  CUtensorMap kvmap{};
+  bool paged = false;
+  dp.num_slots = a.num_blocks * a.block_size;
+  EncodeTiled encode = tensor_map_encoder();
+  if (encode != nullptr && (a.block_size % kTile) == 0 && 2 * dp.num_slots < ((int64_t)1 << 31) &&
+      ((uintptr_t)a.cache % 16) == 0) {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)(2 * dp.num_slots), (cuuint64_t)(2 * a.num_kv_heads)};
+    const cuuint64_t strides[2] = {(cuuint64_t)a.num_kv_heads * kHeadRow, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kTile, (cuuint32_t)(2 * dp.heads_per_cta)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt = a.dtype == MVB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    paged = encode(&kvmap, dt, 3, const_cast<void*>(a.cache), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  if (paged) smem_bytes = kStages * 2 * kTile * dp.heads_per_cta * kHeadRow + 1024;
+  const DecodeKernel fn = a.dtype == MVB_DTYPE_F16 ? kernel_for<__half>(hook, paged)
+                                                   : kernel_for<__nv_bfloat16>(hook, paged);
+  fn<<<grid, threads, smem_bytes, a.stream>>>(kvmap, dp);
   return check_launch();
 }
 

@@ -854,12 +854,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------ host side
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encoder() { return tensor_map_encoder(); }
 
-EncodeTiled encoder() {
+}  // namespace
+
+EncodeTiled tensor_map_encoder() {
   static EncodeTiled fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -872,6 +871,8 @@ EncodeTiled encoder() {
   });
   return fn;
 }
+
+namespace {
 
 // Per-device host state of the prefill kernel, filled under one lock (host
 // threads driving different devices may call at the same time).
