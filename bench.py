@@ -60,8 +60,8 @@ POOL_FRACTION = 0.8
 # to the launch it times.
 # ncu dram read+write bytes of one paged_prefill_kernel launch on the config-3
 # prefill chunks (same seeds, 1 GB pool).
-PREFILL_TRAFFIC = {"fp16": 396.8e6}
-DECODE_TRAFFIC_RATIO = {"config2": (2.527153 + 0.011768) / 2.5180, "config4": 1.6174 / 1.6100}
+PREFILL_TRAFFIC = {"fp16": 396.8e6, "bf16": 339.023e6 + 46.738e6}
+DECODE_TRAFFIC_RATIO = {"config2": (2.527153 + 0.011768) / 2.5180, "config4": (1.613162 + 0.007385) / 1.6100}
 
 
 class DecodeShape:
