@@ -2,7 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--dtype fp16|bf16] [--ctx uniform|fixed4096]
-                    [--workload decode|llama8b|mixed]
+                    [--workload decode|llama8b|mixed|prologue|sample|metadata|engine]
+                    [--no-engine] [--no-engine-baselines] [--no-triton]
 
 Workload (Qwen3-0.6B attention shape): 256 decode
 sequences per GPU, context lengths uniform in [512, 4096] (or all 4096),
@@ -19,6 +20,18 @@ sum(ctx) * Hkv * D * 2 (K and V) * elsize + Q and O (2 * B * Hq * D * elsize)
 + block-table entries (8 B per page).  Inputs are larger than L2 (about
 2.4 GB of KV per step against a 126 MB L2), so no flush is needed.
 
+The same line also carries ``reference_gpu`` (the reference's own Triton
+kernel, ``triton_paged_attention``, timed against this step on the same batch
+in interleaved CUDA-event samples; fp16 only) and ``engine``: BASELINE config
+5, output tokens/s of the reference's own engine (scheduler, KV block manager,
+engine loop, Qwen3 model, installed under baseline/_ref) with ``b200_paged``
+and ``B200ModelRunner``, on a random-init Qwen3-0.6B in fp16: 512 requests,
+prompts U[128,1024], 256 greedy output tokens each, partitioned over the
+ranks (strong scaling, ``engine.value``), plus each rank serving its own 512
+requests at N > 1 (weak scaling, ``engine.weak``); at N = 1 the reference's
+fastest engine configuration (``triton_paged`` with CUDA graphs) runs the
+same job (``engine.reference_engine``).
+
 ``--impl reference`` times the reference algorithm on the host CPU (the
 numpy port in oracle/, all host threads) on a bounded sample of the same
 workload and reports the same metric.
@@ -32,7 +45,8 @@ prologue`` times the fused Qwen3 q/k-norm + RoPE + KV-write kernel on one
 8192-token step (config 5's max_num_batched_tokens) in GB/s; ``--workload
 sample`` the batched sampler on 256 rows of a 151936-token vocabulary (GB/s
 of logits); ``--workload metadata`` the device build of a config-2 step's
-metadata (us per step, lower is better).
+metadata (us per step, lower is better); ``--workload engine`` the config-5
+measurement alone.
 """
 
 from __future__ import annotations

@@ -14,9 +14,9 @@
 // precomputed (the caller evaluates the reference's own expression), so the
 // angles are the reference's bit for bit.
 //
-// One warp per token: it evaluates the token's rotation angles once, then
-// walks its rows — the Hq query heads, the Hkv key heads, the Hkv value
-// heads — in batches of 8 loaded together.  A lane owns columns 2l, 2l+1 and
+// One warp per token: it copies the token's Hkv value rows to the cache with
+// one 8-byte word per lane and row, evaluates its rotation angles once, then
+// walks its Hq query and Hkv key rows in batches of 8 loaded together.  A lane owns columns 2l, 2l+1 and
 // 2l+64, 2l+65 of the 128-element row, so rotate_half's partner of every
 // column is in the same lane; the 8 rows of a batch share one transposed
 // warp reduction of their statistics.
@@ -112,15 +112,6 @@ __device__ __forceinline__ float reduce8_transposed(const float (&s)[8], int lan
   return v;
 }
 
-// Row r of token t: the query heads, then the key heads, then the value heads.
-__device__ __forceinline__ const char* row_of(const PrologueParams& p, int64_t t, int r) {
-  if (r < p.num_q_heads) return p.q + (t * p.q_st + (int64_t)r * p.q_sh) * 2;
-  r -= p.num_q_heads;
-  if (r < p.num_kv_heads) return p.k + (t * p.k_st + (int64_t)r * p.k_sh) * 2;
-  r -= p.num_kv_heads;
-  return p.v + (t * p.v_st + (int64_t)r * p.v_sh) * 2;
-}
-
 template <typename T>
 __global__ void __launch_bounds__(32 * kPrologueWarps)
     qk_prologue_kernel(const PrologueParams p) {
@@ -128,13 +119,36 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kPrologueWarps + (threadIdx.x >> 5);
   if (t >= p.num_tokens) return;
-  const int rows = p.num_q_heads + 2 * p.num_kv_heads;
   const int qk_rows = p.num_q_heads + p.num_kv_heads;
 
   const int64_t slot = __ldg(p.slots + t);
   const bool write = slot >= 0 && slot < p.num_slots;
   if (slot >= p.num_slots && lane == 0 && p.status != nullptr)
     atomicOr(p.status, MVB_STATUS_SLOT_OUT_OF_RANGE);
+
+  // The token's row bases, once: rows then differ by a head stride.
+  constexpr int64_t kRowBytes = kPrologueDim * 2;
+  const char* qbase = p.q + t * p.q_st * 2;
+  const char* kbase = p.k + t * p.k_st * 2;
+  const char* vbase = p.v + t * p.v_st * 2;
+  char* qout = p.q_out + t * p.num_q_heads * kRowBytes;
+  char* kcache = p.cache + (write ? slot : 0) * p.num_kv_heads * kRowBytes;
+  char* vcache = p.cache + (p.num_slots + (write ? slot : 0)) * p.num_kv_heads * kRowBytes;
+
+  // Value rows go to plane 1 unchanged: one 8-byte word per lane and row
+  // (a whole row per instruction), up to 8 rows in flight.
+  if (write) {
+    for (int h0 = 0; h0 < p.num_kv_heads; h0 += kRowsPerWarp) {
+      const int nr = min(kRowsPerWarp, p.num_kv_heads - h0);
+      uint2 w[kRowsPerWarp];
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i)
+        if (i < nr) w[i] = __ldg(reinterpret_cast<const uint2*>(vbase + (int64_t)(h0 + i) * p.v_sh * 2) + lane);
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i)
+        if (i < nr) reinterpret_cast<uint2*>(vcache + (h0 + i) * kRowBytes)[lane] = w[i];
+    }
+  }
 
   // Lane l owns columns 2l, 2l+1 (word l of the row) and 2l+64, 2l+65 (word
   // l+32): rotate_half pairs column c with c + 64, so both partners sit in
@@ -153,15 +167,18 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
   const uint32_t qw_lo = __ldg(qw + lane), qw_hi = __ldg(qw + 32 + lane);
   const uint32_t kw_lo = __ldg(kw + lane), kw_hi = __ldg(kw + 32 + lane);
 
-  for (int r0 = 0; r0 < rows; r0 += kRowsPerWarp) {
-    const int nr = min(kRowsPerWarp, rows - r0);
-    // A batch of rows in flight at once.
+  // Query rows, then key rows, in batches of 8 loaded together.
+  for (int r0 = 0; r0 < qk_rows; r0 += kRowsPerWarp) {
+    const int nr = min(kRowsPerWarp, qk_rows - r0);
     uint32_t lo[kRowsPerWarp], hi[kRowsPerWarp];
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i) {
       lo[i] = hi[i] = 0;
       if (i < nr) {
-        const uint32_t* row = reinterpret_cast<const uint32_t*>(row_of(p, t, r0 + i));
+        const int r = r0 + i;
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(
+            r < p.num_q_heads ? qbase + (int64_t)r * p.q_sh * 2
+                              : kbase + (int64_t)(r - p.num_q_heads) * p.k_sh * 2);
         lo[i] = __ldg(row + lane);
         hi[i] = __ldg(row + 32 + lane);
       }
@@ -182,15 +199,6 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
       const float inv_rms = __shfl_sync(0xffffffffu, inv_lane, 4 * i);
       if (i >= nr) break;
       const int r = r0 + i;
-      if (r >= qk_rows) {  // value row: straight into plane 1
-        if (write) {
-          uint32_t* dst = reinterpret_cast<uint32_t*>(
-              p.cache + ((p.num_slots + slot) * p.num_kv_heads + (r - qk_rows)) * (int64_t)kPrologueDim * 2);
-          dst[lane] = lo[i];
-          dst[32 + lane] = hi[i];
-        }
-        continue;
-      }
       const bool is_q = r < p.num_q_heads;
       // The normalised value rounded to the model dtype, times the weight
       // (one correctly rounded 16-bit product, as the fp32 product rounded).
@@ -205,13 +213,9 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
                                          __fadd_rn(__fmul_rn(ya.y, cs[1]), __fmul_rn(-yb.y, sn[1])));
       const uint32_t out_hi = P::from_f2(__fadd_rn(__fmul_rn(yb.x, cs[0]), __fmul_rn(ya.x, sn[0])),
                                          __fadd_rn(__fmul_rn(yb.y, cs[1]), __fmul_rn(ya.y, sn[1])));
-      uint32_t* dst = nullptr;
-      if (is_q)
-        dst = reinterpret_cast<uint32_t*>(p.q_out + ((t * p.num_q_heads + r) * (int64_t)kPrologueDim) * 2);
-      else if (write)
-        dst = reinterpret_cast<uint32_t*>(p.cache + (slot * p.num_kv_heads + (r - p.num_q_heads)) *
-                                                        (int64_t)kPrologueDim * 2);
-      if (dst != nullptr) {
+      if (is_q || write) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(
+            is_q ? qout + r * kRowBytes : kcache + (r - p.num_q_heads) * kRowBytes);
         dst[lane] = out_lo;
         dst[32 + lane] = out_hi;
       }
