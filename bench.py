@@ -1016,13 +1016,13 @@ def run_prologue(args) -> None:
     clocks = ClockSampler(dev.index)
     clocks.start()
     def timed(fn) -> float:
-        # The flush, then a ~100 us spin that keeps the GPU busy while the
-        # host enqueues the start event and the launch: the events bracket
-        # the kernel, not the host's launch path.
+        # The flush, then a ~0.5 ms spin that keeps the GPU busy while the
+        # host enqueues the start event, runs the Python wrapper and
+        # launches: the events bracket the kernel, not the host's launch path.
         total = 0.0
         for _ in range(args.steps):
             flush.max()
-            torch.cuda._sleep(200_000)
+            torch.cuda._sleep(1_000_000)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             fn()
@@ -1109,7 +1109,7 @@ def run_sample(args) -> None:
     total = 0.0
     for _ in range(args.steps):
         flush.max()
-        torch.cuda._sleep(200_000)  # GPU busy while the host enqueues the event and the launch
+        torch.cuda._sleep(1_000_000)  # ~0.5 ms: GPU busy while the host enqueues the event and the launch
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         step()

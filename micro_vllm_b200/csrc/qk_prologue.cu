@@ -14,12 +14,16 @@
 // precomputed (the caller evaluates the reference's own expression), so the
 // angles are the reference's bit for bit.
 //
-// One warp per token: it copies the token's Hkv value rows to the cache with
-// one 8-byte word per lane and row, evaluates its rotation angles once, then
-// walks its Hq query and Hkv key rows in batches of 8 loaded together.  A lane owns columns 2l, 2l+1 and
-// 2l+64, 2l+65 of the 128-element row, so rotate_half's partner of every
-// column is in the same lane; the 8 rows of a batch share one transposed
-// warp reduction of their statistics.
+// One warp per token.  It copies the token's Hkv value rows to the cache (16
+// bytes per lane, two rows per instruction), evaluates its rotation angles
+// once, then walks its Hq query rows and its Hkv key rows in batches of 8
+// loaded together.  A lane owns columns 2l, 2l+1 and 2l+64, 2l+65 of the
+// 128-element row, so rotate_half's partner of every column is in the same
+// lane; the 8 rows of a batch share one transposed warp reduction of their
+// statistics.  The fp32 arithmetic runs on packed pairs (mul/sub/add/fma
+// .rn.f32x2: each half rounded as the scalar op), which halves the
+// instructions of the norm and the rotation; the kernel is issue-bound
+// without them.
 // Roofline: HBM; bytes per token = (Hq + 2 Hkv) * D * elsize read +
 // (Hq + 2 Hkv) * D * elsize written.
 #include <cuda_bf16.h>
@@ -28,6 +32,7 @@
 
 #include "mvb_common.cuh"
 #include "mvb_internal.h"
+#include "ptx_sm100.cuh"
 
 namespace mvb {
 namespace {
@@ -112,41 +117,109 @@ __device__ __forceinline__ float reduce8_transposed(const float (&s)[8], int lan
   return v;
 }
 
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  sm100::f32x2_unpack(v, r.x, r.y);
+  return r;
+}
+
+// n rows (head stride `sh` bytes from `src`) normalised with weight words
+// (w_lo, w_hi), rotated, and stored to consecutive 256-byte rows at `dst`.
+template <typename T>
+__device__ __forceinline__ void norm_rope_rows(const char* src, int64_t sh, int n, char* dst, bool store,
+                                               uint32_t w_lo, uint32_t w_hi, uint64_t cs, uint64_t sn,
+                                               float eps, int lane) {
+  using P = Pair<T>;
+  for (int r0 = 0; r0 < n; r0 += kRowsPerWarp) {
+    const int nr = min(kRowsPerWarp, n - r0);
+    uint32_t lo[kRowsPerWarp], hi[kRowsPerWarp];
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      lo[i] = hi[i] = 0;
+      if (i < nr) {
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(src + (int64_t)(r0 + i) * sh);
+        lo[i] = __ldg(row + lane);
+        hi[i] = __ldg(row + 32 + lane);
+      }
+    }
+    // RMSNorm statistics of the batch's rows: per-lane sums of squares
+    // (fp32), then one transposed warp reduction and one reciprocal root per
+    // lane for all 8 rows; row i's factor is then read from lane 4i.
+    float ss[kRowsPerWarp];
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
+      const uint64_t av = sm100::f32x2_pack(a.x, a.y), bv = sm100::f32x2_pack(b.x, b.y);
+      const float2 s2 = unpack2(sm100::f32x2_fma(bv, bv, sm100::f32x2_mul(av, av)));
+      ss[i] = s2.x + s2.y;
+    }
+    const float tot = reduce8_transposed(ss, lane);
+    const float inv_lane = 1.0f / sqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / kPrologueDim), eps));
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const float inv_rms = __shfl_sync(0xffffffffu, inv_lane, 4 * i);
+      if (i >= nr) break;
+      const uint64_t inv2 = sm100::f32x2_pack(inv_rms, inv_rms);
+      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
+      // The normalised value rounded to the model dtype, times the weight
+      // (one correctly rounded 16-bit product).
+      const float2 na = unpack2(sm100::f32x2_mul(sm100::f32x2_pack(a.x, a.y), inv2));
+      const float2 nb = unpack2(sm100::f32x2_mul(sm100::f32x2_pack(b.x, b.y), inv2));
+      const float2 ya = P::to_f2(P::mul(P::from_f2(na.x, na.y), w_lo));
+      const float2 yb = P::to_f2(P::mul(P::from_f2(nb.x, nb.y), w_hi));
+      const uint64_t yav = sm100::f32x2_pack(ya.x, ya.y), ybv = sm100::f32x2_pack(yb.x, yb.y);
+      // x * cos + rotate_half(x) * sin, products and sums rounded separately.
+      const float2 o_lo = unpack2(sm100::f32x2_sub(sm100::f32x2_mul(yav, cs), sm100::f32x2_mul(ybv, sn)));
+      const float2 o_hi = unpack2(sm100::f32x2_add(sm100::f32x2_mul(ybv, cs), sm100::f32x2_mul(yav, sn)));
+      if (store) {
+        uint32_t* d = reinterpret_cast<uint32_t*>(dst + (int64_t)(r0 + i) * (kPrologueDim * 2));
+        d[lane] = P::from_f2(o_lo.x, o_lo.y);
+        d[32 + lane] = P::from_f2(o_hi.x, o_hi.y);
+      }
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(32 * kPrologueWarps)
     qk_prologue_kernel(const PrologueParams p) {
-  using P = Pair<T>;
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kPrologueWarps + (threadIdx.x >> 5);
   if (t >= p.num_tokens) return;
-  const int qk_rows = p.num_q_heads + p.num_kv_heads;
 
   const int64_t slot = __ldg(p.slots + t);
   const bool write = slot >= 0 && slot < p.num_slots;
   if (slot >= p.num_slots && lane == 0 && p.status != nullptr)
     atomicOr(p.status, MVB_STATUS_SLOT_OUT_OF_RANGE);
 
-  // The token's row bases, once: rows then differ by a head stride.
   constexpr int64_t kRowBytes = kPrologueDim * 2;
-  const char* qbase = p.q + t * p.q_st * 2;
-  const char* kbase = p.k + t * p.k_st * 2;
   const char* vbase = p.v + t * p.v_st * 2;
-  char* qout = p.q_out + t * p.num_q_heads * kRowBytes;
   char* kcache = p.cache + (write ? slot : 0) * p.num_kv_heads * kRowBytes;
   char* vcache = p.cache + (p.num_slots + (write ? slot : 0)) * p.num_kv_heads * kRowBytes;
 
-  // Value rows go to plane 1 unchanged: one 8-byte word per lane and row
-  // (a whole row per instruction), up to 8 rows in flight.
+  // Value rows go to plane 1 unchanged: 16 bytes per lane, two rows per
+  // instruction when the rows are 16-byte aligned, else 8 bytes per lane.
   if (write) {
-    for (int h0 = 0; h0 < p.num_kv_heads; h0 += kRowsPerWarp) {
-      const int nr = min(kRowsPerWarp, p.num_kv_heads - h0);
-      uint2 w[kRowsPerWarp];
+    const int64_t vsh = p.v_sh * 2;
+    if (((reinterpret_cast<uintptr_t>(vbase) | (uintptr_t)vsh | reinterpret_cast<uintptr_t>(vcache)) & 15) == 0) {
+      const int half = lane >> 4, col = lane & 15;
+      for (int h0 = 0; h0 < p.num_kv_heads; h0 += 8) {
+        uint4 w[4];
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
-        if (i < nr) w[i] = __ldg(reinterpret_cast<const uint2*>(vbase + (int64_t)(h0 + i) * p.v_sh * 2) + lane);
+        for (int i = 0; i < 4; ++i) {
+          const int h = h0 + 2 * i + half;
+          if (h < p.num_kv_heads) w[i] = __ldg(reinterpret_cast<const uint4*>(vbase + h * vsh) + col);
+        }
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
-        if (i < nr) reinterpret_cast<uint2*>(vcache + (h0 + i) * kRowBytes)[lane] = w[i];
+        for (int i = 0; i < 4; ++i) {
+          const int h = h0 + 2 * i + half;
+          if (h < p.num_kv_heads) reinterpret_cast<uint4*>(vcache + h * kRowBytes)[col] = w[i];
+        }
+      }
+    } else {
+      for (int h = 0; h < p.num_kv_heads; ++h)
+        reinterpret_cast<uint2*>(vcache + h * kRowBytes)[lane] =
+            __ldg(reinterpret_cast<const uint2*>(vbase + h * vsh) + lane);
     }
   }
 
@@ -162,65 +235,13 @@ __global__ void __launch_bounds__(32 * kPrologueWarps)
       sincosf(ang, &sn[i], &cs[i]);
     }
   }
+  const uint64_t csv = sm100::f32x2_pack(cs[0], cs[1]), snv = sm100::f32x2_pack(sn[0], sn[1]);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(p.q_w);
   const uint32_t* kw = reinterpret_cast<const uint32_t*>(p.k_w);
-  const uint32_t qw_lo = __ldg(qw + lane), qw_hi = __ldg(qw + 32 + lane);
-  const uint32_t kw_lo = __ldg(kw + lane), kw_hi = __ldg(kw + 32 + lane);
-
-  // Query rows, then key rows, in batches of 8 loaded together.
-  for (int r0 = 0; r0 < qk_rows; r0 += kRowsPerWarp) {
-    const int nr = min(kRowsPerWarp, qk_rows - r0);
-    uint32_t lo[kRowsPerWarp], hi[kRowsPerWarp];
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      lo[i] = hi[i] = 0;
-      if (i < nr) {
-        const int r = r0 + i;
-        const uint32_t* row = reinterpret_cast<const uint32_t*>(
-            r < p.num_q_heads ? qbase + (int64_t)r * p.q_sh * 2
-                              : kbase + (int64_t)(r - p.num_q_heads) * p.k_sh * 2);
-        lo[i] = __ldg(row + lane);
-        hi[i] = __ldg(row + 32 + lane);
-      }
-    }
-    // RMSNorm statistics of the batch's rows: per-lane sums of squares
-    // (fp32), then one transposed warp reduction and one reciprocal root per
-    // lane for all 8 rows; row i's factor is then read from lane 4i.
-    float ss[kRowsPerWarp];
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
-      ss[i] = (a.x * a.x + a.y * a.y) + (b.x * b.x + b.y * b.y);
-    }
-    const float tot = reduce8_transposed(ss, lane);
-    const float inv_lane = 1.0f / sqrtf(__fadd_rn(__fmul_rn(tot, 1.0f / kPrologueDim), p.eps));
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const float inv_rms = __shfl_sync(0xffffffffu, inv_lane, 4 * i);
-      if (i >= nr) break;
-      const int r = r0 + i;
-      const bool is_q = r < p.num_q_heads;
-      // The normalised value rounded to the model dtype, times the weight
-      // (one correctly rounded 16-bit product, as the fp32 product rounded).
-      const float2 a = P::to_f2(lo[i]), b = P::to_f2(hi[i]);
-      const float2 ya = P::to_f2(P::mul(P::from_f2(__fmul_rn(a.x, inv_rms), __fmul_rn(a.y, inv_rms)),
-                                        is_q ? qw_lo : kw_lo));
-      const float2 yb = P::to_f2(P::mul(P::from_f2(__fmul_rn(b.x, inv_rms), __fmul_rn(b.y, inv_rms)),
-                                        is_q ? qw_hi : kw_hi));
-      // x * cos + rotate_half(x) * sin, products and sum rounded separately:
-      // column c < 64 takes -x[c + 64], column c + 64 takes x[c].
-      const uint32_t out_lo = P::from_f2(__fadd_rn(__fmul_rn(ya.x, cs[0]), __fmul_rn(-yb.x, sn[0])),
-                                         __fadd_rn(__fmul_rn(ya.y, cs[1]), __fmul_rn(-yb.y, sn[1])));
-      const uint32_t out_hi = P::from_f2(__fadd_rn(__fmul_rn(yb.x, cs[0]), __fmul_rn(ya.x, sn[0])),
-                                         __fadd_rn(__fmul_rn(yb.y, cs[1]), __fmul_rn(ya.y, sn[1])));
-      if (is_q || write) {
-        uint32_t* dst = reinterpret_cast<uint32_t*>(
-            is_q ? qout + r * kRowBytes : kcache + (r - p.num_q_heads) * kRowBytes);
-        dst[lane] = out_lo;
-        dst[32 + lane] = out_hi;
-      }
-    }
-  }
+  norm_rope_rows<T>(p.q + t * p.q_st * 2, p.q_sh * 2, p.num_q_heads, p.q_out + t * p.num_q_heads * kRowBytes,
+                    true, __ldg(qw + lane), __ldg(qw + 32 + lane), csv, snv, p.eps, lane);
+  norm_rope_rows<T>(p.k + t * p.k_st * 2, p.k_sh * 2, p.num_kv_heads, kcache, write, __ldg(kw + lane),
+                    __ldg(kw + 32 + lane), csv, snv, p.eps, lane);
 }
 
 }  // namespace
