@@ -262,6 +262,30 @@ MVB_API int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows,
                        int64_t* out_tokens, void* stream);
 
 /*
+ * mvb_sample with the reference's random stream for chosen rows.
+ *
+ * torch.multinomial(probabilities, 1, generator), as the reference's
+ * _sample_row calls it (src/micro_vllm/sampling/sampler.py:52-61), picks the
+ * token that maximises probability / q, q = torch.empty_like(probabilities)
+ * .exponential_(1, generator) — an exponential race.  A row r with
+ * 0 <= noise_row[r] < num_noise_rows takes that race over its kept set with
+ * q = noise + noise_row[r] * noise_row_stride (float32, vocab values, drawn
+ * by the caller from a generator seeded as the reference seeds it); the
+ * probability is exp(x - max x), x = logit / temperature in fp32 (the
+ * softmax denominator is common to all tokens), so the token is the
+ * reference's unless its two best ratios agree to within fp32 rounding.
+ * Other rows draw as mvb_sample.  noise may be NULL (every row draws as
+ * mvb_sample); otherwise noise_row (device int32 [num_rows]) must be given
+ * and noise_row_stride >= vocab.  Greedy rows ignore their noise row.
+ */
+MVB_API int mvb_sample_with_noise(const void* logits, int64_t row_stride, int64_t num_rows,
+                                  int64_t vocab, int32_t dtype, const float* temperature,
+                                  const int32_t* top_k, const float* top_p, const uint64_t* seed,
+                                  const int64_t* sample_index, const float* noise,
+                                  int64_t noise_row_stride, int64_t num_noise_rows,
+                                  const int32_t* noise_row, int64_t* out_tokens, void* stream);
+
+/*
  * Device-side build of one step's attention metadata (one cache group).
  *
  * Replaces the host loops of ModelRunner._flatten_model_input,

@@ -84,6 +84,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _P],
     ),
+    "mvb_sample_with_noise": (
+        ctypes.c_int,
+        [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P],
+    ),
     "mvb_build_metadata": (
         ctypes.c_int,
         [

@@ -208,12 +208,16 @@ int mvb_qk_norm_rope_and_cache(const void* query, const int64_t* q_strides, cons
   return launch_qk_prologue(a);
 }
 
-int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
-               int32_t dtype, const float* temperature, const int32_t* top_k, const float* top_p,
-               const uint64_t* seed, const int64_t* sample_index, int64_t* out_tokens,
-               void* stream) {
+int mvb_sample_with_noise(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
+                          int32_t dtype, const float* temperature, const int32_t* top_k,
+                          const float* top_p, const uint64_t* seed, const int64_t* sample_index,
+                          const float* noise, int64_t noise_row_stride, int64_t num_noise_rows,
+                          const int32_t* noise_row, int64_t* out_tokens, void* stream) {
   if (elem_bytes_of(dtype) == 0) return MVB_ERR_UNSUPPORTED_DTYPE;
   if (num_rows < 0 || vocab <= 0 || vocab >= ((int64_t)1 << 31) || row_stride < 0)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (noise != nullptr && (noise_row == nullptr || noise_row_stride < vocab || num_noise_rows < 0 ||
+                           num_noise_rows > INT32_MAX))
     return MVB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return MVB_OK;
   if (!logits || !temperature || !top_k || !top_p || !seed || !sample_index || !out_tokens)
@@ -230,8 +234,20 @@ int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t
   a.seed = seed;
   a.sample_index = sample_index;
   a.out_tokens = out_tokens;
+  a.noise = num_noise_rows > 0 ? noise : nullptr;
+  a.noise_stride = noise_row_stride;
+  a.num_noise_rows = num_noise_rows;
+  a.noise_row = noise_row;
   a.stream = static_cast<cudaStream_t>(stream);
   return launch_sample(a);
+}
+
+int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t vocab,
+               int32_t dtype, const float* temperature, const int32_t* top_k, const float* top_p,
+               const uint64_t* seed, const int64_t* sample_index, int64_t* out_tokens,
+               void* stream) {
+  return mvb_sample_with_noise(logits, row_stride, num_rows, vocab, dtype, temperature, top_k, top_p,
+                               seed, sample_index, nullptr, 0, 0, nullptr, out_tokens, stream);
 }
 
 int mvb_build_metadata(const int32_t* num_computed_tokens, const int32_t* num_scheduled_tokens,

@@ -141,6 +141,10 @@ struct SampleArgs {
   const uint64_t* seed;
   const int64_t* sample_index;
   int64_t* out_tokens;
+  const float* noise;        // NULL: every stochastic row takes the Philox draw
+  int64_t noise_stride;
+  int64_t num_noise_rows;    // noise_row entries outside [0, num_noise_rows): Philox draw
+  const int32_t* noise_row;
   cudaStream_t stream;
 };
 int launch_sample(const SampleArgs& a);

@@ -17,7 +17,10 @@
 // "Parallel random numbers: as easy as 1, 2, 3", SC 2011) keyed by the row's
 // seed with the row's sample index as counter, so a (seed, sample index)
 // pair always gives the same token whatever the other rows are; the stream
-// is this sampler's own, not torch's.
+// is this sampler's own, not torch's.  A row given Exp(1) noise instead
+// (drawn by the caller from a generator seeded as the reference seeds its
+// own) ends in the exponential race torch.multinomial runs: the kept token
+// with the largest exp(x - max) / noise.
 //
 // One CTA of 512 threads per row; the row is read in tiles of 4096 tokens
 // (16-byte loads, 8 consecutive tokens per thread, so a tile is in index
@@ -81,6 +84,10 @@ struct SampleParams {
   const uint64_t* seed;
   const int64_t* sample_index;
   int64_t* out;
+  const float* noise;        // Exp(1) noise rows, or NULL
+  int64_t noise_stride;      // elements between noise rows
+  int32_t num_noise_rows;
+  const int32_t* noise_row;  // per row: its noise row; outside [0, num_noise_rows): none
 };
 
 struct SampleSmem {
@@ -525,6 +532,21 @@ __device__ __forceinline__ int64_t cand_index(unsigned long long c) {
   return (int64_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull));
 }
 
+// Exponential race, the form torch.multinomial(probabilities, 1, generator)
+// takes: the token that maximises p / q, q the row's Exp(1) noise drawn by
+// the caller from the reference's generator.  p = exp(x - max x) with x =
+// logit / T in fp32, as the reference's filtered logits; its softmax
+// denominator is common to every token, so leaving it out can change the
+// winner only where the two best ratios agree to within fp32 rounding.
+// Packed as a candidate: the largest entry is the largest ratio, lowest
+// index first, as torch.argmax.
+__device__ __forceinline__ unsigned long long race_entry(float l, float temp, float xm, const float* q,
+                                                         int64_t i) {
+  const float x = __fdiv_rn(l, temp);
+  const float r = __fdiv_rn(expf(x - xm), __ldg(q + i));
+  return cand_of(order_key(r), i);
+}
+
 __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams p) {
   extern __shared__ __align__(16) unsigned char sample_smem_raw[];
   SampleSmem& s = *reinterpret_cast<SampleSmem*>(sample_smem_raw);
@@ -565,6 +587,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
   const bool use_k = k_req > 0 && (int64_t)k_req < V;
   const float top_p = p.top_p[row];
   const bool use_p = top_p < 1.f;
+  // A row with noise ends in an exponential race over its kept set instead
+  // of the Philox draw.
+  const int32_t nrow = p.noise != nullptr ? p.noise_row[row] : -1;
+  const float* qn = nrow >= 0 && nrow < p.num_noise_rows ? p.noise + (int64_t)nrow * p.noise_stride : nullptr;
 
   // ---- pass 1: max, and the top-k digit histogram ------------------------
   if (use_k)
@@ -590,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
   const float c1 = __fdiv_rn(1.4426950408889634f, temp);  // log2(e) / T
   const float c2 = mx * c1;
   const float s1 = __fdiv_rn(kMassBinScale, temp);
+  const float xm = __fdiv_rn(mx, temp);  // the largest x (division by T > 0 is monotone)
   __syncthreads();
 
   // Index of the rank-th token (index order) whose key satisfies `hit`; used
@@ -717,6 +744,21 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
       }
       __syncthreads();
       keep = (int)max(s.found, 1ll);  // the top token is always kept
+    }
+    if (qn != nullptr) {
+      unsigned long long best = 0;
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {
+        const int i = tid * kPer + q;
+        if (i < keep) {
+          const unsigned long long e = s.cand[i];
+          const unsigned long long r = race_entry(key_value((uint32_t)(e >> 32)), temp, xm, qn, cand_index(e));
+          best = r > best ? r : best;
+        }
+      }
+      best = block_max_u64(best, s);
+      if (tid == 0) p.out[row] = cand_index(best);
+      return;
     }
     unsigned long long kmine = 0;
 #pragma unroll
@@ -1043,6 +1085,24 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const SampleParams 
     return !cut_p || key > p_key || (key == p_key && i <= p_last);
   };
 
+  // ---- exponential race over the kept tokens (rows with noise) ------------
+  if (qn != nullptr) {
+    unsigned long long best = 0;
+    for_each_tile(rd, tid, [&](const int64_t i0, const float (&v)[kVec], const int n) {
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) {
+        const float x = v[j];
+        if (j < n && kept(order_key(x), i0 + j)) {
+          const unsigned long long r = race_entry(x, temp, xm, qn, i0 + j);
+          best = r > best ? r : best;
+        }
+      }
+    });
+    best = block_max_u64(best, s);
+    if (tid == 0) p.out[row] = cand_index(best);
+    return;
+  }
+
   // ---- draw: inverse CDF over the kept tokens, thread-major order ---------
   // The draw orders tokens by thread: thread t's tokens (tile by tile, 8 at a
   // time) before thread t+1's.  Each thread's kept mass is summed (the mass
@@ -1129,6 +1189,10 @@ int launch_sample(const SampleArgs& a) {
   p.seed = a.seed;
   p.sample_index = a.sample_index;
   p.out = a.out_tokens;
+  p.noise = a.noise;
+  p.noise_stride = a.noise_stride;
+  p.num_noise_rows = (int32_t)a.num_noise_rows;
+  p.noise_row = a.noise_row;
   if (a.num_rows > INT32_MAX) return MVB_ERR_UNSUPPORTED_SHAPE;
   const int smem = (int)sizeof(SampleSmem);
   cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

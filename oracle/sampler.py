@@ -46,3 +46,19 @@ def kept_and_probabilities(
     m = x[kept].max()
     probs = np.where(kept, np.exp((x - m).astype(np.float64)), 0.0)
     return kept, probs / probs.sum()
+
+
+def race_token(logits: np.ndarray, temperature: float, kept: np.ndarray, q: np.ndarray) -> int:
+    """The token ``torch.multinomial(probabilities, 1, generator)`` returns
+    (sampler.py:55-61), restated as the exponential race torch runs for one
+    sample: argmax(probabilities / q), q = ``empty_like(probabilities)
+    .exponential_(1, generator)``, the first index among equal ratios.
+    probabilities = exp(x - max x) over the kept set with x = logit / T in
+    fp32; the softmax denominator is common to every token and is left out
+    (the winner changes only where the two best ratios agree to within
+    fp32 rounding)."""
+
+    x = np.asarray(logits, np.float32) / np.float32(temperature)
+    m = x[kept].max()
+    e = np.where(kept, np.exp((x - m).astype(np.float32)), np.float32(0.0)).astype(np.float32)
+    return int(np.argmax(e / np.asarray(q, np.float32)))

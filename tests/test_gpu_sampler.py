@@ -5,7 +5,11 @@
 * stochastic rows: every draw lies in the set the reference's top-k / top-p
   filters keep (golden), and the empirical distribution of many draws matches
   the oracle's probabilities (a chi-square bound at fixed seeds);
-* a (seed, sample index) pair gives the same token whatever the other rows.
+* a (seed, sample index) pair gives the same token whatever the other rows;
+* rows with Exp(1) noise run torch.multinomial's exponential race: the
+  oracle's token on every kernel path, and with the noise drawn from
+  generators seeded as the reference seeds its own, the reference Sampler's
+  token ids.
 """
 
 from __future__ import annotations
@@ -177,3 +181,85 @@ def test_exact_ties_beyond_the_shared_memory_set() -> None:
     assert got.max() <= 5000 and got.max() > 1000
     got = sample_tokens(logits, *_rows(rows, 1.0, 3000, 0.1, seed=3)).cpu().numpy()
     assert got.max() <= 300  # top-k 3000, then 10 % of its mass: indices 0..300
+
+
+def _cuda_noise(seeds_and_indices, vocab):
+    """Exp(1) rows as the reference's torch.multinomial draws them: one
+    generator on the logits' device per row, seeded (seed + index) mod 2^63."""
+
+    noise = torch.empty((len(seeds_and_indices), vocab), dtype=torch.float32, device=DEV)
+    for r, (seed, index) in enumerate(seeds_and_indices):
+        g = torch.Generator(device=DEV)
+        g.manual_seed((seed + index) % 2**63)
+        noise[r].exponential_(1.0, generator=g)
+    return noise
+
+
+@pytest.mark.parametrize(
+    "policy",
+    ["temperature", "top_k_small", "top_p", "k_and_p", "large_k", "flat_top_p", "k_and_p_large"],
+)
+def test_noise_rows_run_the_exponential_race_of_the_oracle(policy) -> None:
+    """mvb_sample_with_noise: a row with noise returns oracle.race_token over
+    the reference's kept set, on every path of the kernel (the shared-memory
+    candidate sets and the whole-row passes); rows without noise still draw
+    from their kept set."""
+
+    from oracle.sampler import race_token
+
+    temp, k, p, scale, vocab = {
+        "temperature": (0.8, 0, 1.0, 3.0, 151936),
+        "top_k_small": (1.0, 50, 1.0, 3.0, 151936),
+        "top_p": (1.1, 0, 0.9, 3.0, 151936),
+        "k_and_p": (0.9, 40, 0.9, 3.0, 151936),
+        "large_k": (1.0, 3000, 1.0, 1.0, 50000),
+        "flat_top_p": (1.0, 0, 0.5, 0.05, 50000),
+        "k_and_p_large": (1.0, 20000, 0.7, 0.05, 50000),
+    }[policy]
+    rows = 12
+    g = torch.Generator(device=DEV).manual_seed(41)
+    logits = (torch.randn((rows, vocab), generator=g, device=DEV) * scale).to(torch.bfloat16)
+    pairs = [(1000 + 7 * r, 3 * r) for r in range(rows)]
+    noise = _cuda_noise(pairs[: rows // 2 * 2 : 2], vocab)  # even rows only
+    noise_row = torch.tensor([r // 2 if r % 2 == 0 else -1 for r in range(rows)], dtype=torch.int32, device=DEV)
+    args = _rows(rows, temp, k, p, seed=5)
+    got = sample_tokens(logits, *args, noise=noise, noise_row=noise_row).cpu().numpy()
+    host, q = logits.float().cpu().numpy(), noise.cpu().numpy()
+    for r in range(rows):
+        kept, _ = kept_and_probabilities(host[r], temp, k or None, p)
+        assert kept[got[r]], (policy, r)
+        if r % 2 == 0:
+            assert got[r] == race_token(host[r], temp, kept, q[r // 2]), (policy, r)
+    with pytest.raises(ValueError):
+        sample_tokens(logits, *args, noise=noise, noise_row=None)
+
+
+def test_seeded_rows_give_the_reference_sampler_tokens() -> None:
+    """The reference's own Sampler (torch.multinomial with its seeded CUDA
+    generator) and B200Sampler on the same Qwen3-vocabulary logits: every
+    greedy and every seeded stochastic row gets the same token id.  fp32
+    logits: with bf16's 256 values per octave, equal logits at a top-k
+    boundary are common, and torch.topk keeps an unspecified one of them."""
+
+    from _reference import require_reference
+
+    require_reference()
+    from micro_vllm.sampling.params import SamplingParams
+    from micro_vllm.sampling.sampler import Sampler
+
+    rows, vocab = 40, 151936
+    g = torch.Generator(device=DEV).manual_seed(8)
+    logits = torch.randn((rows, vocab), generator=g, device=DEV) * 2.5
+    policies = [(0.0, None, 1.0), (0.7, None, 1.0), (1.0, 50, 1.0), (1.2, None, 0.9), (0.9, 40, 0.8)]
+    params = tuple(
+        SamplingParams(max_tokens=8, temperature=t, top_k=k, top_p=p, seed=None if t == 0.0 else 31 * r + 2**40)
+        for r, (t, k, p) in ((r, policies[r % len(policies)]) for r in range(rows))
+    )
+    ids = tuple(f"req{r}" for r in range(rows))
+    indices = tuple(5 * r + 1 for r in range(rows))
+    want = [t.token_id for t in Sampler()(logits, ids, params, indices).sampled_tokens]
+    got = [t.token_id for t in B200Sampler()(logits, ids, params, indices).sampled_tokens]
+    assert got == want
+    # Without the reference's streams the tokens are the kernel's own draws.
+    own = [t.token_id for t in B200Sampler(reference_streams=False)(logits, ids, params, indices).sampled_tokens]
+    assert own != want

@@ -372,6 +372,34 @@ def test_sampler_oracle_reference_test_cases() -> None:
     assert kept.all()
 
 
+def test_race_oracle_is_torch_multinomial_with_the_same_generator() -> None:
+    """oracle.sampler.race_token with q drawn by a generator seeded as the
+    reference seeds its own equals torch.multinomial(probabilities, 1,
+    generator) on the reference's filtered softmax (sampler.py:48-61), for
+    every policy.  (CPU generator here; the GPU tests run the CUDA one.)"""
+
+    import torch
+
+    from oracle.sampler import race_token
+
+    rng = np.random.default_rng(5)
+    vocab = 6000
+    for trial in range(60):
+        logits = (rng.standard_normal(vocab) * rng.uniform(0.5, 4.0)).astype(np.float32)
+        temp, k, p = [(0.8, None, 1.0), (1.0, 40, 1.0), (1.3, None, 0.9), (0.7, 500, 0.95)][trial % 4]
+        kept, _ = kept_and_probabilities(logits, temp, k, p)
+        x = torch.from_numpy(logits) / temp
+        probs = torch.softmax(x.masked_fill(~torch.from_numpy(kept), -torch.inf), dim=-1)
+        seed = (2**62 + 977 * trial) % 2**63
+        g = torch.Generator()
+        g.manual_seed(seed)
+        want = int(torch.multinomial(probs, num_samples=1, generator=g).item())
+        g = torch.Generator()
+        g.manual_seed(seed)
+        q = torch.empty_like(probs).exponential_(1, generator=g).numpy()
+        assert race_token(logits, temp, kept, q) == want, trial
+
+
 # ---------------------------------------------------------------- metadata build
 from _golden import BlockIds, PlanRequest, load_metadata_case, metadata_manifest  # noqa: E402
 from oracle.metadata import PlannedRequest  # noqa: E402
