@@ -185,6 +185,17 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout: float = 10.0) -> None:
+        """Block until the first sample has arrived (bounded): nvidia-smi
+        takes up to seconds to start, longer with one per rank, and a timed
+        region of a few milliseconds would otherwise end before it."""
+
+        end = time.monotonic() + timeout
+        while self.proc is not None and not self.lines and time.monotonic() < end:
+            if self.proc.poll() is not None:
+                return
+            time.sleep(0.02)
+
     def stop(self) -> dict:
         if self.proc is not None:
             time.sleep(0.25)
@@ -478,6 +489,7 @@ def run_ours(args) -> dict:
     # ---- timed region: K full forward steps ----
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.wait_first()
     t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     # A ~100 us spin keeps the GPU busy while the host enqueues the start
@@ -928,6 +940,7 @@ def run_mixed(args) -> None:
     op(prefill_only.query, prefill_only.key, prefill_only.value, prefill_only.cache, prefill_only.metadata)
     clocks = ClockSampler(dev.index)
     clocks.start()
+    clocks.wait_first()
     prefill_ms = timed(lambda: attention_only(prefill_only, out_p), args.steps)
     mixed_ms = timed(lambda: op(mixed.query, mixed.key, mixed.value, mixed.cache, mixed.metadata), args.steps)
     clock_info = clocks.stop()
@@ -1015,6 +1028,7 @@ def run_prologue(args) -> None:
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev.index)
     clocks.start()
+    clocks.wait_first()
     def timed(fn) -> float:
         # The flush, then a ~0.5 ms spin that keeps the GPU busy while the
         # host enqueues the start event, runs the Python wrapper and
@@ -1106,6 +1120,7 @@ def run_sample(args) -> None:
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev.index)
     clocks.start()
+    clocks.wait_first()
     total = 0.0
     for _ in range(args.steps):
         flush.max()
@@ -1275,6 +1290,7 @@ def run_metadata(args) -> None:
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev.index)
     clocks.start()
+    clocks.wait_first()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     graph.replay()
