@@ -22,7 +22,9 @@ sum(ctx) * Hkv * D * 2 (K and V) * elsize + Q and O (2 * B * Hq * D * elsize)
 
 The same line also carries ``reference_gpu`` (the reference's own Triton
 kernel, ``triton_paged_attention``, timed against this step on the same batch
-in interleaved CUDA-event samples; fp16 only) and ``engine``: BASELINE config
+in interleaved CUDA-event samples; fp16 only), ``reference_sdpa`` (the
+reference's SDPA backend, ``paged_sdpa_attention``, on the same batch) and
+``engine``: BASELINE config
 5, output tokens/s of the reference's own engine (scheduler, KV block manager,
 engine loop, Qwen3 model, installed under baseline/_ref) with ``b200_paged``
 and ``B200ModelRunner``, on a random-init Qwen3-0.6B in fp16: 512 requests,
@@ -127,7 +129,8 @@ def parse_args() -> argparse.Namespace:
                     help="decode: BASELINE config 2 (headline, with the config-5 engine object); "
                          "mixed: config 3 (prefill + decode); engine: config 5 alone")
     ap.add_argument("--no-triton", action="store_true",
-                    help="skip the reference's Triton kernel timed beside ours on the decode batch")
+                    help="skip the reference's GPU backends (Triton kernel, SDPA) timed beside ours "
+                         "on the decode batch")
     ap.add_argument("--no-engine", action="store_true",
                     help="decode workload without the config-5 engine measurement")
     ap.add_argument("--engine-requests", type=int, default=512)
@@ -411,6 +414,63 @@ def triton_comparator(batch, ours, dev, samples: int = 10, launches: int = 5) ->
     }
 
 
+def sdpa_comparator(batch, ours, dev, calls: int = 3, launches: int = 10) -> dict:
+    """The reference's SDPA backend on the same batch and pool:
+    ``paged_sdpa_attention`` (src/micro_vllm/attention/operators/sdpa.py:82-114
+    in the reference project: its KV write, a gather of each request's
+    history with host reads per request, then one PyTorch SDPA call per
+    request).  The path synchronises the host per request, so each call is
+    timed whole with CUDA events (median of ``calls``); ``ours`` is timed
+    beside it as the median of ``launches`` back-to-back steps."""
+
+    import statistics as st
+
+    import torch
+
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    try:
+        from micro_vllm.attention.operators.sdpa import paged_sdpa_attention
+    except Exception as exc:  # micro_vllm missing
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+
+    md = batch.metadata
+
+    def theirs():
+        return paged_sdpa_attention(batch.query, batch.key, batch.value, batch.cache, md)
+
+    out_ref, out_ours = theirs(), ours()
+    torch.cuda.synchronize(dev)
+    diff = (out_ref.float() - out_ours.float()).abs().max().item()
+    del out_ref
+    times = []
+    for _ in range(calls):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        theirs()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    mine = []
+    for _ in range(launches):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ours()
+        b.record()
+        b.synchronize()
+        mine.append(a.elapsed_time(b))
+    t_theirs, t_ours = st.median(times), st.median(mine)
+    return {
+        "impl": "paged_sdpa_attention, the reference's SDPA backend (KV write, per-request gather, "
+                "PyTorch SDPA per request)",
+        "ms_per_step": t_theirs,
+        "ours_ms_per_step": t_ours,
+        "speedup_ours_over_sdpa": t_theirs / t_ours,
+        "max_abs_diff_vs_ours": diff,
+        "method": f"CUDA events around whole calls (host-synchronised per request), medians of "
+                  f"{calls} calls and of {launches} steps of ours",
+    }
+
+
 def run_ours(args) -> dict:
     import torch
     import torch.distributed as dist
@@ -515,10 +575,13 @@ def run_ours(args) -> dict:
     attn_ms = max_over_ranks(a_start.elapsed_time(a_stop) / args.steps)
 
     # ---- the reference's own GPU kernel on the same batch (rank 0) ----
-    comparator = None
+    comparator = sdpa = None
     if rank == 0 and not args.no_triton:
         comparator = triton_comparator(batch, step, dev)
         torch.cuda.synchronize(dev)
+        sdpa = sdpa_comparator(batch, step, dev)
+        torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
     barrier()
 
     # ---- end to end through the public operator with host buffers ----
@@ -659,6 +722,11 @@ def run_ours(args) -> dict:
             comparator["value"] = attn_bytes / (comparator["ms_per_step"] * 1e-3) / 1e9
             comparator["unit"] = "GB/s"
         line["reference_gpu"] = comparator
+    if sdpa is not None:
+        if "ms_per_step" in sdpa:
+            sdpa["value"] = attn_bytes / (sdpa["ms_per_step"] * 1e-3) / 1e9
+            sdpa["unit"] = "GB/s"
+        line["reference_sdpa"] = sdpa
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, elsize, args.cpu_sample_seconds)
     return line
