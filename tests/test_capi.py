@@ -84,6 +84,21 @@ def test_argument_checks_return_before_touching_the_device(lib) -> None:
         0, 0, 16, 1.0, 0, None, 0, None, None,
     )
     assert rc == _lib.MVB_OK
+    # Sampler noise: rows without noise_row, or noise rows shorter than the
+    # vocabulary, are rejected before anything runs; no rows is a no-op.
+    fake = ctypes.c_void_p(16)
+    rc = lib.mvb_sample_with_noise(None, 0, 1, 100, 0, None, None, None, None, None,
+                                   fake, 100, 1, None, None, None)
+    assert rc == _lib.MVB_ERR_INVALID_ARGUMENT
+    rc = lib.mvb_sample_with_noise(None, 0, 1, 100, 0, None, None, None, None, None,
+                                   fake, 99, 1, fake, None, None)
+    assert rc == _lib.MVB_ERR_INVALID_ARGUMENT
+    rc = lib.mvb_sample_with_noise(None, 0, 0, 100, 0, None, None, None, None, None,
+                                   None, 0, 0, None, None, None)
+    assert rc == _lib.MVB_OK
+    rc = lib.mvb_sample_with_noise(None, 0, 1, 100, 9, None, None, None, None, None,
+                                   None, 0, 0, None, None, None)
+    assert rc == _lib.MVB_ERR_UNSUPPORTED_DTYPE
 
 
 def test_operator_rejects_cpu_tensors() -> None:
