@@ -286,6 +286,39 @@ MVB_API int mvb_sample_with_noise(const void* logits, int64_t row_stride, int64_
                                   const int32_t* noise_row, int64_t* out_tokens, void* stream);
 
 /*
+ * RMSNorm of a Qwen3 decoder layer, optionally after its residual add, in
+ * one launch (the reference model runs each as a chain of torch kernels).
+ *
+ * Replaces RMSNorm.forward (src/micro_vllm/layers/normalization.py:15-22)
+ * and, with residual, the `residual + hidden_states` before it
+ * (src/micro_vllm/models/qwen.py:151-154).  x [num_rows, hidden] with row
+ * stride x_row_stride (elements), unit column stride; weight [hidden]; all
+ * of dtype (MVB_DTYPE_F16 or _BF16).  With residual (same layout, its own
+ * row stride) the row is h = x + residual rounded to dtype, written to
+ * sum_out [num_rows, hidden] contiguous; without it h = x.  out [num_rows,
+ * hidden] contiguous receives weight * dtype(h * 1/sqrt(mean(h^2) + eps)),
+ * the statistics in fp32.  hidden and both row strides must be multiples of
+ * 8 and the pointers 16-byte aligned (else MVB_ERR_UNSUPPORTED_SHAPE).
+ */
+MVB_API int mvb_rms_norm(const void* x, int64_t x_row_stride, const void* residual,
+                         int64_t residual_row_stride, void* sum_out, void* out, const void* weight,
+                         float eps, int64_t num_rows, int32_t hidden, int32_t dtype, void* stream);
+
+/*
+ * silu(gate) * up of a SwiGLU MLP in one launch.
+ *
+ * Replaces `F.silu(gate_proj(h))` times `up_proj(h)` in SwiGLUMLP.forward
+ * (src/micro_vllm/layers/mlp.py:19-21) for one projection that computes both:
+ * gate_up [num_rows, >= 2 * intermediate] with row stride gate_up_row_stride
+ * holds the gate columns then the up columns.  out [num_rows, intermediate]
+ * contiguous receives dtype(dtype(silu(gate)) * up), silu in fp32.
+ * intermediate and the row stride must be multiples of 8 and the pointers
+ * 16-byte aligned.
+ */
+MVB_API int mvb_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out,
+                         int64_t num_rows, int32_t intermediate, int32_t dtype, void* stream);
+
+/*
  * Device-side build of one step's attention metadata (one cache group).
  *
  * Replaces the host loops of ModelRunner._flatten_model_input,

@@ -84,6 +84,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _P],
     ),
+    "mvb_rms_norm": (
+        ctypes.c_int,
+        [_P, _I64, _P, _I64, _P, _P, _P, _F32, _I64, _I32, _I32, _P],
+    ),
+    "mvb_silu_mul": (
+        ctypes.c_int,
+        [_P, _I64, _P, _I64, _I32, _I32, _P],
+    ),
     "mvb_sample_with_noise": (
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P],

@@ -250,6 +250,49 @@ int mvb_sample(const void* logits, int64_t row_stride, int64_t num_rows, int64_t
                                seed, sample_index, nullptr, 0, 0, nullptr, out_tokens, stream);
 }
 
+int mvb_rms_norm(const void* x, int64_t x_row_stride, const void* residual, int64_t residual_row_stride,
+                 void* sum_out, void* out, const void* weight, float eps, int64_t num_rows, int32_t hidden,
+                 int32_t dtype, void* stream) {
+  if (dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_rows < 0 || hidden <= 0 || x_row_stride < hidden ||
+      (residual != nullptr && (residual_row_stride < hidden || sum_out == nullptr)))
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return MVB_OK;
+  if (!x || !out || !weight) return MVB_ERR_INVALID_ARGUMENT;
+  RmsNormArgs a;
+  a.x = x;
+  a.x_stride = x_row_stride;
+  a.residual = residual;
+  a.r_stride = residual_row_stride;
+  a.sum_out = sum_out;
+  a.out = out;
+  a.weight = weight;
+  a.eps = eps;
+  a.rows = num_rows;
+  a.hidden = hidden;
+  a.dtype = dtype;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_rms_norm(a);
+}
+
+int mvb_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t num_rows,
+                 int32_t intermediate, int32_t dtype, void* stream) {
+  if (dtype != MVB_DTYPE_F16 && dtype != MVB_DTYPE_BF16) return MVB_ERR_UNSUPPORTED_DTYPE;
+  if (num_rows < 0 || intermediate <= 0 || gate_up_row_stride < 2 * (int64_t)intermediate)
+    return MVB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return MVB_OK;
+  if (!gate_up || !out) return MVB_ERR_INVALID_ARGUMENT;
+  SiluMulArgs a;
+  a.gate_up = gate_up;
+  a.gu_stride = gate_up_row_stride;
+  a.out = out;
+  a.rows = num_rows;
+  a.inter = intermediate;
+  a.dtype = dtype;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return launch_silu_mul(a);
+}
+
 int mvb_build_metadata(const int32_t* num_computed_tokens, const int32_t* num_scheduled_tokens,
                        const int32_t* num_block_ids, const int32_t* block_ids,
                        const uint8_t* requires_sampling, const int32_t* input_token_ids,

@@ -149,6 +149,33 @@ struct SampleArgs {
 };
 int launch_sample(const SampleArgs& a);
 
+struct RmsNormArgs {
+  const void* x;
+  int64_t x_stride;       // elements between rows
+  const void* residual;   // NULL: no residual add
+  int64_t r_stride;
+  void* sum_out;          // x + residual, [rows, hidden] contiguous
+  void* out;              // [rows, hidden] contiguous
+  const void* weight;     // [hidden]
+  float eps;
+  int64_t rows;
+  int32_t hidden;
+  int32_t dtype;
+  cudaStream_t stream;
+};
+int launch_rms_norm(const RmsNormArgs& a);
+
+struct SiluMulArgs {
+  const void* gate_up;    // [rows, >= 2 * inter]: gate columns then up columns
+  int64_t gu_stride;
+  void* out;              // [rows, inter] contiguous
+  int64_t rows;
+  int32_t inter;
+  int32_t dtype;
+  cudaStream_t stream;
+};
+int launch_silu_mul(const SiluMulArgs& a);
+
 struct MetadataArgs {
   const int32_t* num_computed;
   const int32_t* num_scheduled;

@@ -17,10 +17,17 @@ three host-side stages of its step with this package's kernels:
 * in Qwen3 layers, ``q_norm``, ``k_norm``, the rotary embedding and the
   operator's KV write (models/qwen.py:89-98) become one
   ``mvb_qk_norm_rope_and_cache`` launch, followed by attention over the cache
-  (``B200PagedAttentionOperator.attend``).
+  (``B200PagedAttentionOperator.attend``);
+* with ``fused_layers``, the rest of each Qwen3 decoder layer
+  (models/qwen.py:136-156) runs in fewer launches: every RMSNorm as one
+  ``mvb_rms_norm`` (the post-attention one together with the residual add
+  before it), q/k/v as one GEMM over their weights concatenated, gate/up as
+  one GEMM and ``mvb_silu_mul`` (layers/mlp.py:19-21).  The reference's
+  Linear modules keep working: their weights become views into the
+  concatenated ones.
 
-The scheduler, KV block manager, request state, engine loop, model layers
-other than attention and the GEMMs are the reference's, unchanged.
+The scheduler, KV block manager, request state, engine loop and the GEMMs
+are the reference's, unchanged.
 ``B200Worker`` is the reference ``Worker`` around a ``B200ModelRunner``
 (``build_worker``); ``fresh_engine`` assembles
 ``Engine(Scheduler, SingleProcessExecutor(worker))`` as ``LLM.__init__`` does
@@ -52,6 +59,7 @@ from micro_vllm.worker.model_runner import ModelRunner, _CudaGraphExecution
 from micro_vllm.worker.worker import Worker
 
 from micro_vllm_b200.integration import register
+from micro_vllm_b200.layers import rms_norm, silu_mul
 from micro_vllm_b200.metadata import DeviceMetadataBuilder
 from micro_vllm_b200.operators import B200PagedAttentionOperator
 from micro_vllm_b200.prologue import Qwen3AttentionPrologue
@@ -65,6 +73,7 @@ class RunnerOptions:
     device_metadata: bool = True
     device_sampler: bool = True
     fused_prologue: bool = True
+    fused_layers: bool = True
 
 
 class B200ModelRunner(ModelRunner):
@@ -84,6 +93,8 @@ class B200ModelRunner(ModelRunner):
         super().initialize_model()
         if self._options.fused_prologue:
             self._install_prologue()
+            if self._options.fused_layers:
+                self._install_fused_layers()
 
     def _b200_operators(self) -> list[B200PagedAttentionOperator]:
         seen: dict[int, B200PagedAttentionOperator] = {}
@@ -111,6 +122,46 @@ class B200ModelRunner(ModelRunner):
             module._b200_prologue = Qwen3AttentionPrologue.from_modules(
                 module.q_norm, module.k_norm, module.rotary_embedding)
             module.forward = types.MethodType(_qwen3_attention_forward, module)
+
+    def _install_fused_layers(self) -> None:
+        """Fewer launches per Qwen3 decoder layer (module docstring), for
+        layers whose attention runs the fused prologue, in fp16 / bf16, with
+        bias-free projections and 16-bit norm weights of the model's dtype."""
+
+        try:
+            from micro_vllm.layers.normalization import RMSNorm
+            from micro_vllm.models.qwen import Qwen3DecoderLayer
+        except ImportError:
+            return
+        dtype = self._dtype
+
+        def fusable_norm(norm) -> bool:
+            w = norm.weight
+            return w.dtype == dtype and w.dim() == 1 and w.shape[0] % 8 == 0
+
+        with torch.no_grad():
+            for layer in self._model.modules():
+                if not isinstance(layer, Qwen3DecoderLayer):
+                    continue
+                attn, mlp = layer.self_attn, layer.mlp
+                if getattr(attn, "_b200_prologue", None) is None:
+                    continue
+                projections = (attn.q_proj, attn.k_proj, attn.v_proj, mlp.gate_proj, mlp.up_proj)
+                if any(getattr(m, "bias", None) is not None for m in projections):
+                    continue
+                if not (fusable_norm(layer.input_layernorm) and fusable_norm(layer.post_attention_layernorm)):
+                    continue
+                if mlp.gate_proj.weight.shape[0] % 8 != 0:
+                    continue
+                attn._b200_qkv = _concatenate_weights(attn.q_proj, attn.k_proj, attn.v_proj)
+                mlp._b200_gate_up = _concatenate_weights(mlp.gate_proj, mlp.up_proj)
+                mlp._b200_inter = int(mlp.gate_proj.weight.shape[0])
+                attn.forward = types.MethodType(_qwen3_attention_forward_qkv, attn)
+                layer.forward = types.MethodType(_qwen3_layer_forward, layer)
+            for norm in self._model.modules():
+                if isinstance(norm, RMSNorm) and fusable_norm(norm):
+                    norm.forward = types.MethodType(_rms_norm_forward, norm)
+        torch.cuda.empty_cache()
 
     # -- step inputs ---------------------------------------------------------
     def _layer_specs(self) -> list:
@@ -200,6 +251,56 @@ def _qwen3_attention_forward(self, hidden_states, positions, layer_kv_cache, met
     query = self._b200_prologue(positions, query, key, value, layer_kv_cache, metadata)
     attention_output = self.attention.operator.attend(query, layer_kv_cache, metadata)
     return self.o_proj(attention_output.flatten(start_dim=1))
+
+
+def _concatenate_weights(*linears) -> torch.Tensor:
+    """One [sum of out features, in features] weight; each module's weight
+    becomes a view of its rows, so the concatenation costs no memory."""
+
+    joined = torch.cat([m.weight.data for m in linears], dim=0)
+    row = 0
+    for m in linears:
+        n = m.weight.shape[0]
+        m.weight.data = joined[row:row + n]
+        row += n
+    return joined
+
+
+def _rms_norm_forward(self, hidden_states):
+    """``RMSNorm.forward`` (layers/normalization.py:15-22) as one launch."""
+
+    shape = hidden_states.shape
+    out, _ = rms_norm(hidden_states.reshape(-1, shape[-1]), self.weight, self.variance_epsilon)
+    return out.view(shape)
+
+
+def _qwen3_attention_forward_qkv(self, hidden_states, positions, layer_kv_cache, metadata):
+    """``_qwen3_attention_forward`` with q, k and v from one GEMM over the
+    concatenated projection weights (views of its output feed the prologue)."""
+
+    qkv = torch.nn.functional.linear(hidden_states, self._b200_qkv)
+    nq = self.num_attention_heads * self.head_dim
+    nk = self.num_key_value_heads * self.head_dim
+    query = qkv[:, :nq].view(-1, self.num_attention_heads, self.head_dim)
+    key = qkv[:, nq:nq + nk].view(-1, self.num_key_value_heads, self.head_dim)
+    value = qkv[:, nq + nk:nq + 2 * nk].view(-1, self.num_key_value_heads, self.head_dim)
+    query = self._b200_prologue(positions, query, key, value, layer_kv_cache, metadata)
+    attention_output = self.attention.operator.attend(query, layer_kv_cache, metadata)
+    return self.o_proj(attention_output.flatten(start_dim=1))
+
+
+def _qwen3_layer_forward(self, hidden_states, positions, layer_kv_cache, metadata):
+    """``Qwen3DecoderLayer.forward`` (models/qwen.py:136-156): the same sums,
+    norms and products, in fewer launches."""
+
+    x = self.input_layernorm(hidden_states)
+    attention = self.self_attn(x, positions, layer_kv_cache, metadata)
+    # residual + attention, and the post-attention norm of it, in one launch.
+    norm = self.post_attention_layernorm
+    x, hidden = rms_norm(attention, norm.weight, norm.variance_epsilon, residual=hidden_states)
+    mlp = self.mlp
+    gate_up = torch.nn.functional.linear(x, mlp._b200_gate_up)
+    return hidden + mlp.down_proj(silu_mul(gate_up, mlp._b200_inter))
 
 
 class B200Worker(Worker):
