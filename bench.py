@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--dtype fp16|bf16] [--ctx uniform|fixed4096]
-                    [--workload decode|llama8b|mixed|prologue|sample|metadata|engine]
+                    [--workload decode|llama8b|mixed|prologue|layers|sample|metadata|engine]
                     [--no-engine] [--no-engine-baselines] [--no-triton]
 
 Workload (Qwen3-0.6B attention shape): 256 decode
@@ -124,7 +124,7 @@ def parse_args() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--workload",
-                    choices=("decode", "mixed", "llama8b", "prologue", "sample", "metadata", "engine"),
+                    choices=("decode", "mixed", "llama8b", "prologue", "layers", "sample", "metadata", "engine"),
                     default="decode",
                     help="decode: BASELINE config 2 (headline, with the config-5 engine object); "
                          "mixed: config 3 (prefill + decode); engine: config 5 alone")
@@ -1058,6 +1058,74 @@ def run_mixed(args) -> None:
 
 
 # ---------------------------------------------------------------- prologue
+def run_layers(args) -> None:
+    """The fused decoder-layer stages (mvb_rms_norm with the residual add,
+    mvb_silu_mul) on an 8192-token step of the Qwen3-0.6B shape (hidden
+    1024, intermediate 3072), fp16 unless --dtype; each timed alone, the L2
+    evicted before every timed launch."""
+
+    import torch
+
+    from micro_vllm_b200.layers import rms_norm, silu_mul
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    tokens, hidden, inter = 8192, 1024, 3072
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn((tokens, hidden), generator=g, device=dev).to(dtype)
+    residual = torch.randn((tokens, hidden), generator=g, device=dev).to(dtype)
+    weight = (0.5 + torch.rand(hidden, generator=g, device=dev)).to(dtype)
+    gate_up = torch.randn((tokens, 2 * inter), generator=g, device=dev).to(dtype)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB read between launches
+    ops = {
+        "rms_norm_add": (lambda: rms_norm(x, weight, 1e-6, residual=residual), 4 * tokens * hidden * 2),
+        "silu_mul": (lambda: silu_mul(gate_up, inter), 3 * tokens * inter * 2),
+    }
+    for fn, _ in ops.values():
+        for _ in range(max(args.warmup, 3)):
+            fn()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    clocks.wait_first()
+    results = {}
+    for name, (fn, byts) in ops.items():
+        total = 0.0
+        for _ in range(args.steps):
+            flush.max()
+            torch.cuda._sleep(1_000_000)  # ~0.5 ms: the GPU stays busy while the host launches
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            total += a.elapsed_time(b)
+        ms = total / args.steps
+        results[name] = {"ms": ms, "bytes": byts, "GBps": byts / (ms * 1e-3) / 1e9}
+    clock_info = clocks.stop()
+    peak, peak_src = _hbm_peak()
+    all_bytes = sum(r["bytes"] for r in results.values())
+    all_ms = sum(r["ms"] for r in results.values())
+    value = all_bytes / (all_ms * 1e-3) / 1e9
+    line = {
+        "metric": "fused_layer_stages_GBps", "value": value, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": all_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dtype == torch.float16 else "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"RMSNorm after the residual add and silu(gate) * up, {tokens} tokens, "
+                               f"hidden {hidden}, intermediate {inter} (one Qwen3-0.6B layer's stages)",
+                   "l2": "L2 evicted (256 MB read) before every timed launch"},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                     "traffic": None, "peak_source": peak_src, "kernels": {
+                         name: {"GBps": r["GBps"], "frac": r["GBps"] / peak, "ms": r["ms"],
+                                "bytes_per_launch": r["bytes"]} for name, r in results.items()}},
+        "gpu_launches": 2 * args.steps, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_prologue(args) -> None:
     """Fused q/k RMSNorm + RoPE + KV write (mvb_qk_norm_rope_and_cache) on an
     8192-token step at the Qwen3-0.6B attention shape, fp16 unless --dtype."""
@@ -1429,6 +1497,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "mixed":
         run_mixed(args)
+    elif args.workload == "layers":
+        run_layers(args)
     elif args.workload == "prologue":
         run_prologue(args)
     elif args.workload == "sample":
