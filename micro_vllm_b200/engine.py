@@ -20,8 +20,9 @@ three host-side stages of its step with this package's kernels:
   (``B200PagedAttentionOperator.attend``);
 * with ``fused_layers``, the rest of each Qwen3 decoder layer
   (models/qwen.py:136-156) runs in fewer launches: every RMSNorm as one
-  ``mvb_rms_norm`` (the post-attention one together with the residual add
-  before it), q/k/v as one GEMM over their weights concatenated, gate/up as
+  ``mvb_rms_norm`` together with the residual add before it (the model's
+  layer loop, models/qwen.py:220-240, carries each layer's last add into the
+  next norm), q/k/v as one GEMM over their weights concatenated, gate/up as
   one GEMM and ``mvb_silu_mul`` (layers/mlp.py:19-21).  The reference's
   Linear modules keep working: their weights become views into the
   concatenated ones.
@@ -161,6 +162,15 @@ class B200ModelRunner(ModelRunner):
             for norm in self._model.modules():
                 if isinstance(norm, RMSNorm) and fusable_norm(norm):
                     norm.forward = types.MethodType(_rms_norm_forward, norm)
+            # With every layer fused, each layer's last residual add moves
+            # into the next layer's input norm (and the last one into the
+            # final norm): one launch fewer per layer.
+            model = self._model
+            layers = list(getattr(model, "layers", ()))
+            if (layers and all(getattr(layer.mlp, "_b200_gate_up", None) is not None for layer in layers)
+                    and isinstance(getattr(model, "norm", None), RMSNorm) and fusable_norm(model.norm)
+                    and hasattr(model, "embed_tokens")):
+                model.forward = types.MethodType(_qwen3_model_forward, model)
         torch.cuda.empty_cache()
 
     # -- step inputs ---------------------------------------------------------
@@ -301,6 +311,39 @@ def _qwen3_layer_forward(self, hidden_states, positions, layer_kv_cache, metadat
     mlp = self.mlp
     gate_up = torch.nn.functional.linear(x, mlp._b200_gate_up)
     return hidden + mlp.down_proj(silu_mul(gate_up, mlp._b200_inter))
+
+
+def _qwen3_layer_step(self, hidden_states, pending, positions, layer_kv_cache, metadata):
+    """One fused decoder layer that leaves its MLP output unadded: returns
+    (h, m) with the layer's output h + m; the caller adds them in the next
+    norm.  ``pending`` is the previous layer's m (None for the first)."""
+
+    norm = self.input_layernorm
+    if pending is None:
+        x, hidden = rms_norm(hidden_states, norm.weight, norm.variance_epsilon)
+    else:  # residual + hidden_states of the previous layer (models/qwen.py:156)
+        x, hidden = rms_norm(pending, norm.weight, norm.variance_epsilon, residual=hidden_states)
+    attention = self.self_attn(x, positions, layer_kv_cache, metadata)
+    norm = self.post_attention_layernorm
+    x, hidden = rms_norm(attention, norm.weight, norm.variance_epsilon, residual=hidden)
+    mlp = self.mlp
+    gate_up = torch.nn.functional.linear(x, mlp._b200_gate_up)
+    return hidden, mlp.down_proj(silu_mul(gate_up, mlp._b200_inter))
+
+
+def _qwen3_model_forward(self, input_ids, positions, layer_kv_caches, layer_attention_metadata):
+    """``Qwen3Model.forward`` (models/qwen.py:220-240) over fused layers, the
+    residual adds carried into the following norms."""
+
+    hidden = self.embed_tokens(input_ids)
+    pending = None
+    for layer, layer_kv_cache, metadata in zip(self.layers, layer_kv_caches, layer_attention_metadata,
+                                               strict=True):
+        hidden, pending = _qwen3_layer_step(layer, hidden, pending, positions, layer_kv_cache, metadata)
+    if pending is None:
+        return self.norm(hidden)
+    out, _ = rms_norm(pending, self.norm.weight, self.norm.variance_epsilon, residual=hidden)
+    return out
 
 
 class B200Worker(Worker):
