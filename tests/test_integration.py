@@ -145,3 +145,25 @@ def test_engine_requests_are_seeded():
     assert all(1 <= t <= 151935 for r in a for t in r.prompt_token_ids)
     shards = partition_sequences([len(r.prompt_token_ids) + r.max_tokens for r in a], 8)
     assert sorted(i for s in shards for i in s.indices) == list(range(64))
+
+
+def test_concatenated_projection_weights_are_shared_views(reference):
+    """B200ModelRunner's fused layers run q/k/v (and gate/up) as one GEMM over
+    their weights concatenated; the reference's Linear modules keep their
+    weights as views into that tensor, so values and memory are unchanged."""
+
+    from micro_vllm.layers.linear import Linear
+
+    from micro_vllm_b200.engine import _concatenate_weights
+
+    torch.manual_seed(0)
+    q, k, v = Linear(8, 16, bias=False), Linear(8, 4, bias=False), Linear(8, 4, bias=False)
+    before = [m.weight.detach().clone() for m in (q, k, v)]
+    joined = _concatenate_weights(q, k, v)
+    assert joined.shape == (24, 8)
+    assert torch.equal(joined, torch.cat(before))
+    for m, w in zip((q, k, v), before):
+        assert torch.equal(m.weight, w)
+        assert m.weight.untyped_storage().data_ptr() == joined.untyped_storage().data_ptr()
+    x = torch.randn(3, 8)
+    assert torch.equal(torch.nn.functional.linear(x, joined)[:, 16:20], k(x))
