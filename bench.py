@@ -45,7 +45,9 @@ U[4096,8192], bf16) with the same metric; ``--workload mixed`` is config 3
 and reports the prefill kernel's tensor throughput in TFLOP/s; ``--workload
 prologue`` times the fused Qwen3 q/k-norm + RoPE + KV-write kernel on one
 8192-token step (config 5's max_num_batched_tokens) in GB/s; ``--workload
-sample`` the batched sampler on 256 rows of a 151936-token vocabulary (GB/s
+layers`` the fused decoder-layer stages (RMSNorm after the residual add,
+silu * up) on the same step in GB/s; ``--workload sample`` the batched
+sampler on 256 rows of a 151936-token vocabulary (GB/s
 of logits); ``--workload metadata`` the device build of a config-2 step's
 metadata (us per step, lower is better); ``--workload engine`` the config-5
 measurement alone.
