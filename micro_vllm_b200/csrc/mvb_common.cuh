@@ -58,4 +58,16 @@ __device__ __forceinline__ int64_t find_request(const int64_t* __restrict__ qsl,
   return r;
 }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with
+// programmatic stream serialization may start while the kernel before it in
+// the stream still runs; grid_dependency_wait() returns once that kernel has
+// completed and its writes are visible (at once for a normal launch), and
+// allow_dependent_launch() lets the next such kernel start early.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 }  // namespace mvb

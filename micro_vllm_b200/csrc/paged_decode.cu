@@ -718,11 +718,6 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
   const int32_t rowp = kPaged ? hb * kHeadRow : hb * kHeadRow + 16;
   const int32_t plane_stride = kTile * rowp;
   const int32_t stage_bytes = 2 * plane_stride;
-  const int64_t tiles = p.ctrl[kCtrlTiles];
-  const int64_t n_all = tiles * (p.num_kv_heads / hb);
-  const int64_t grid = gridDim.x;
-  const int64_t first = (int64_t)blockIdx.x * n_all / grid;
-  const int64_t last = ((int64_t)blockIdx.x + 1) * n_all / grid;
   const uint32_t full0 = smem_u32(&bars[0]), empty0 = smem_u32(&bars[kStages]);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -731,7 +726,17 @@ __global__ void __launch_bounds__(32 * (kMaxHeadsPerCta + 1), 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
+  // Launched as a programmatic dependent of the planner: everything above
+  // overlaps its tail; nothing the planner writes is read before this wait.
+  // The prefill pass that follows may then launch as SMs free up.
+  grid_dependency_wait();
+  allow_dependent_launch();
   __syncthreads();
+  const int64_t tiles = p.ctrl[kCtrlTiles];
+  const int64_t n_all = tiles * (p.num_kv_heads / hb);
+  const int64_t grid = gridDim.x;
+  const int64_t first = (int64_t)blockIdx.x * n_all / grid;
+  const int64_t last = ((int64_t)blockIdx.x + 1) * n_all / grid;
   if (first >= last) return;
   const int warp = threadIdx.x >> 5;
   if (warp == hb) {
@@ -907,7 +912,22 @@ int launch_paged_decode(const AttentionProblem& a, const WorkspaceLayout& w, int
   if (paged) smem_bytes = kStages * 2 * kTile * dp.heads_per_cta * kHeadRow + 1024;
   const DecodeKernel fn = a.dtype == MVB_DTYPE_F16 ? kernel_for<__half>(hook, paged)
                                                    : kernel_for<__nv_bfloat16>(hook, paged);
-  fn<<<grid, threads, smem_bytes, a.stream>>>(kvmap, dp);
+  // A programmatic dependent of the planner launched just before it.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, kvmap, dp);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return MVB_ERR_CUDA;
+  }
   return check_launch();
 }
 

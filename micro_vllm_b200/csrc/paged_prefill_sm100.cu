@@ -197,6 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Launched as a programmatic dependent of the decode kernel, which may
+  // still run: this CTA waits for it before anything else, so the pass's
+  // completion implies the decode kernel's (later work reads both outputs).
+  grid_dependency_wait();
   const int64_t n_items = p.ctrl[kCtrlPrefillUnits] * p.num_kv_heads;
 
   if (tid == 0) first_claim = atomicAdd(p.cursor, 1);
@@ -1002,11 +1006,26 @@ int launch_paged_prefill(const AttentionProblem& a, const WorkspaceLayout& w) {
       st.configured = true;
     }
   }
-  const int grid = num_sms();
-  if (a.dtype == MVB_DTYPE_BF16)
-    paged_prefill_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, a.stream>>>(qmap, kvmap, omap, pp);
-  else
-    paged_prefill_kernel<__half><<<grid, kThreads, kSmemBytes, a.stream>>>(qmap, kvmap, omap, pp);
+  // A programmatic dependent of the decode kernel launched just before it:
+  // its CTAs take SMs as decode CTAs leave (each waits for the whole decode
+  // grid first), so the launch overlaps the decode kernel's tail.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)num_sms());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = a.dtype == MVB_DTYPE_BF16
+                            ? cudaLaunchKernelEx(&cfg, paged_prefill_kernel<__nv_bfloat16>, qmap, kvmap, omap, pp)
+                            : cudaLaunchKernelEx(&cfg, paged_prefill_kernel<__half>, qmap, kvmap, omap, pp);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return MVB_ERR_CUDA;
+  }
   return check_launch();
 }
 

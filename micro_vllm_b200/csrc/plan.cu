@@ -102,6 +102,9 @@ __device__ __forceinline__ int64_t block_inclusive_scan(int64_t v, int64_t* warp
 }
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanParams p) {
+  // The decode kernel is launched as a programmatic dependent: it may set up
+  // on the free SMs now and waits for this grid before reading the plan.
+  allow_dependent_launch();
   if (blockIdx.x > 0) {
     // Zero rows of tokens outside [qsl[0], qsl[R]).
     const int64_t covered_lo =
