@@ -167,3 +167,30 @@ def test_concatenated_projection_weights_are_shared_views(reference):
         assert m.weight.untyped_storage().data_ptr() == joined.untyped_storage().data_ptr()
     x = torch.randn(3, 8)
     assert torch.equal(torch.nn.functional.linear(x, joined)[:, 16:20], k(x))
+
+
+def test_seeded_rows_get_the_reference_generators_noise():
+    """B200Sampler draws Exp(1) noise only for seeded stochastic rows, each
+    from a generator seeded (seed + sample index) mod 2^63 on the logits'
+    device, as the reference's _sample_row seeds its own (sampler.py:52-61);
+    greedy rows and rows without a seed get none (noise_row -1)."""
+
+    from micro_vllm_b200.sampling import B200Sampler
+
+    class Params:
+        def __init__(self, temperature, seed):
+            self.temperature, self.top_k, self.top_p, self.seed = temperature, None, 1.0, seed
+
+    vocab = 1000
+    logits = torch.zeros((4, vocab))
+    params = (Params(0.0, 5), Params(0.8, 2**63 - 1), Params(0.8, None), Params(1.0, 7))
+    indices = (3, 4, 5, 6)
+    noise, rows = B200Sampler()._reference_noise(logits, params, indices)
+    assert rows.tolist() == [-1, 0, -1, 1]
+    assert noise.shape == (2, vocab) and noise.dtype == torch.float32
+    for n, (seed, index) in enumerate(((2**63 - 1, 4), (7, 6))):
+        g = torch.Generator()
+        g.manual_seed((seed + index) % 2**63)
+        assert torch.equal(noise[n], torch.empty(vocab).exponential_(1.0, generator=g))
+    assert B200Sampler(reference_streams=False)._reference_noise(logits, params, indices) == (None, None)
+    assert B200Sampler()._reference_noise(logits, params[:1] + params[2:3], indices[:2]) == (None, None)
