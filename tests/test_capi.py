@@ -139,3 +139,17 @@ def test_pinned_staging_needs_cuda() -> None:
         PinnedStaging("cpu")
     with pytest.raises(RuntimeError, match="CUDA device"):
         UploadPipeline("cpu")
+
+
+def test_layer_stages_reject_cpu_tensors() -> None:
+    """The fused layer stages, like the attention operator, have no CPU path."""
+
+    import torch
+
+    from micro_vllm_b200.layers import rms_norm, silu_mul
+
+    x = torch.zeros((2, 64), dtype=torch.float16)
+    with pytest.raises(ValueError):
+        rms_norm(x, torch.ones(64, dtype=torch.float16), 1e-6)
+    with pytest.raises(ValueError):
+        silu_mul(torch.zeros((2, 128), dtype=torch.float16), 64)
