@@ -129,12 +129,14 @@ class B200ModelRunner(ModelRunner):
         layers whose attention runs the fused prologue, in fp16 / bf16, with
         bias-free projections and 16-bit norm weights of the model's dtype."""
 
+        dtype = self._dtype
+        if dtype not in (torch.float16, torch.bfloat16):
+            return  # the fused kernels take 16-bit rows only
         try:
             from micro_vllm.layers.normalization import RMSNorm
             from micro_vllm.models.qwen import Qwen3DecoderLayer
         except ImportError:
             return
-        dtype = self._dtype
 
         def fusable_norm(norm) -> bool:
             w = norm.weight

@@ -99,6 +99,28 @@ def test_greedy_tokens_match_the_reference_operator(env):
         assert got == expected, f"{name} differs from the reference operator"
 
 
+def test_fp32_model_keeps_the_reference_layers(env):
+    """An fp32 model through ``B200ModelRunner``: the fused prologue and layer
+    stages take 16-bit rows only, so none is installed (no RMSNorm module
+    gets a replaced forward) and the model runs the reference's own layers
+    over ``b200_paged``'s exact fp32 path; greedy tokens equal the reference
+    operator's."""
+
+    from micro_vllm_b200.engine import RunnerOptions, build_worker
+
+    path, dev = env["path"], env["device"]
+    reqs = requests(n=3, max_tokens=8)
+    outputs = {}
+    for name, operator, options in (("reference", "reference", None), ("b200_runner", "b200_paged", RunnerOptions())):
+        config = make_config(path, operator, False, torch.float32)
+        worker = build_worker(config, options)
+        if options is not None:
+            model = worker._model_runner._model
+            assert not any("forward" in vars(m) for m in model.modules() if type(m).__name__ == "RMSNorm")
+        outputs[name] = drive(worker, config, reqs, dev)
+    assert outputs["b200_runner"] == outputs["reference"]
+
+
 class ScriptedSampler:
     """Records each row's logits and returns a fixed token per (request, sample
     index), so two runners see the same token streams whatever they compute."""
