@@ -279,10 +279,16 @@ def _concatenate_weights(*linears) -> torch.Tensor:
 
 
 def _rms_norm_forward(self, hidden_states):
-    """``RMSNorm.forward`` (layers/normalization.py:15-22) as one launch."""
+    """``RMSNorm.forward`` (layers/normalization.py:15-22) as one launch; rows
+    the kernel does not take (another dtype than the weight's 16-bit one, an
+    unaligned view) run the reference's own forward."""
 
     shape = hidden_states.shape
-    out, _ = rms_norm(hidden_states.reshape(-1, shape[-1]), self.weight, self.variance_epsilon)
+    rows = hidden_states.reshape(-1, shape[-1])
+    if (hidden_states.dtype != self.weight.dtype or not hidden_states.is_cuda or rows.stride(-1) != 1
+            or rows.stride(0) % 8 != 0 or rows.data_ptr() % 16 != 0):
+        return type(self).forward(self, hidden_states)
+    out, _ = rms_norm(rows, self.weight, self.variance_epsilon)
     return out.view(shape)
 
 

@@ -194,3 +194,24 @@ def test_seeded_rows_get_the_reference_generators_noise():
         assert torch.equal(noise[n], torch.empty(vocab).exponential_(1.0, generator=g))
     assert B200Sampler(reference_streams=False)._reference_noise(logits, params, indices) == (None, None)
     assert B200Sampler()._reference_noise(logits, params[:1] + params[2:3], indices[:2]) == (None, None)
+
+
+def test_patched_rms_norm_falls_back_to_the_reference_forward(reference):
+    """B200ModelRunner replaces RMSNorm.forward with the one-launch kernel;
+    rows that kernel does not take (here: CPU rows) still get the reference's
+    own forward, unchanged."""
+
+    import types
+
+    from micro_vllm.layers.normalization import RMSNorm
+
+    from micro_vllm_b200.engine import _rms_norm_forward
+
+    torch.manual_seed(0)
+    norm = RMSNorm(64, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(0.5 + torch.rand(64))
+    x = torch.randn(5, 3, 64)
+    want = norm(x)
+    norm.forward = types.MethodType(_rms_norm_forward, norm)
+    assert torch.equal(norm(x), want)
